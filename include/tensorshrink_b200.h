@@ -1,0 +1,197 @@
+/*
+ * tensorshrink_b200 — C ABI of the B200 (sm_100a) QuantLinear hot path.
+ *
+ * Plain pointers and sizes only: every pointer argument named "device" is a
+ * CUDA device address on the current device, and `stream` is a cudaStream_t
+ * passed as void* (NULL = legacy default stream). No entry point allocates
+ * device memory; scratch comes from caller-provided workspaces whose sizes
+ * the *_workspace_size() functions report. All launches are asynchronous on
+ * `stream`. Functions return TS_OK (0) or a negative ts_status; the message
+ * of the last failure on the calling thread is in ts_last_error().
+ *
+ * Packed-weight layout is the reference's `QuantLinear` buffer layout,
+ * unchanged (tensorshrink codec.py:102-151, modules.py:337-448):
+ *   packed   uint8 [rows, padded_cols*bits/8]; 4-bit: byte = c[2j] | c[2j+1]<<4;
+ *            2-bit: byte = c[4j] | c[4j+1]<<2 | c[4j+2]<<4 | c[4j+3]<<6; 8-bit raw.
+ *   scale/gmin fp16 [rows, n_groups]   (or the double-quantized form:
+ *   dq_*_codes uint8 flattened row-major over [rows, n_groups], one
+ *   (meta_scale, meta_min) fp16 pair per dq_group_size entries).
+ *   codebook fp32 [1<<bits] (NF / Lloyd-Max levels) or NULL.
+ *   outliers: row-sorted int32 row/col, fp16 delta, plus CSR row offsets.
+ * Reconstruction: w[r,c] = cb?[code] * scale[r,g] + gmin[r,g] (+ delta at
+ * outlier positions), g = c / group_size.
+ */
+#ifndef TENSORSHRINK_B200_H
+#define TENSORSHRINK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TS_API __attribute__((visibility("default")))
+#else
+#define TS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ts_dtype {
+  TS_F16 = 0,
+  TS_BF16 = 1,
+  TS_F32 = 2
+} ts_dtype;
+
+typedef enum ts_status {
+  TS_OK = 0,
+  TS_ERR_INVALID = -1,     /* bad argument (shape, pointer, alignment) */
+  TS_ERR_UNSUPPORTED = -2, /* valid but not covered (bit width, dtype) */
+  TS_ERR_CUDA = -3,        /* a CUDA runtime call failed */
+  TS_ERR_WORKSPACE = -4    /* workspace missing or too small */
+} ts_status;
+
+/* One quantized weight matrix as resident on the device (QuantLinear's
+ * buffers). Exactly one of {scale,gmin} / {dq_*} is set. */
+typedef struct ts_qweight {
+  int64_t rows;             /* out_features (N) */
+  int64_t cols;             /* in_features (K), unpadded */
+  int64_t padded_cols;      /* cols rounded up to a multiple of group_size */
+  int64_t n_groups;         /* padded_cols / group_size */
+  int64_t packed_row_bytes; /* row stride of `packed` in bytes */
+  int32_t bits;             /* 2, 4 or 8 */
+  int32_t group_size;
+  const uint8_t* packed;
+  const uint16_t* scale;    /* fp16 [rows, n_groups] or NULL */
+  const uint16_t* gmin;     /* fp16 [rows, n_groups] or NULL */
+  const uint8_t* dq_scale_codes;
+  const uint16_t* dq_scale_meta; /* fp16 [n_super, 2] */
+  const uint8_t* dq_gmin_codes;
+  const uint16_t* dq_gmin_meta;
+  int32_t dq_group_size;
+  int32_t reserved0;
+  const float* codebook;    /* fp32 [1<<bits] or NULL */
+  int64_t n_outliers;
+  const int32_t* outlier_row_ptr; /* [rows+1] CSR offsets into the tables */
+  const int32_t* outlier_row;     /* row-sorted */
+  const int32_t* outlier_col;
+  const uint16_t* outlier_delta;  /* fp16 */
+} ts_qweight;
+
+/* ---------------------------------------------------------------------------
+ * Fused dequant-GEMM:  out[M, rows] = x[M, cols] . W^T (+ outliers) (+ bias)
+ *
+ * Replaces triton_kernels.py:714-945 `fused_quantized_linear` (and, for
+ * M > 64, the modules.py:898-922 dequantize_weight + F.linear path). Same
+ * arguments in the same meaning; the output is written directly in
+ * `out_dtype` (fp16, bf16 or fp32) instead of an fp32 pool buffer plus a
+ * cast, and outliers are folded into the kernel's epilogue through the CSR
+ * row offsets instead of an atomic post-pass.
+ * x: device [M, cols] rows `x_row_stride` elements apart, fp16 or bf16.
+ * bias: device [rows] in `bias_dtype`, or NULL. out: device [M, rows].
+ * workspace: device memory of ts_qlinear_workspace_size() bytes, zero-filled
+ * before its first use; calls leave it zeroed again. Calls that run
+ * concurrently must use distinct workspaces.
+ */
+TS_API size_t ts_qlinear_workspace_size(const ts_qweight* w, int64_t M);
+
+TS_API int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M,
+               int64_t x_row_stride, const void* bias, int bias_dtype, void* out,
+               int out_dtype, int64_t out_row_stride, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* Standalone outlier correction into an fp32 result:
+ *   out[m, row[k]] += x[m, col[k]] * delta[k]   for every k (any order).
+ * Replaces triton_kernels.py:948-991 `apply_outlier_correction` (the path the
+ * reference takes for unsorted or very large outlier tables). */
+TS_API int ts_apply_outlier_correction(float* out, int64_t M, int64_t N, int64_t out_row_stride,
+                                const void* x, int x_dtype, int64_t x_row_stride,
+                                const int32_t* row, const int32_t* col,
+                                const uint16_t* delta, int64_t n_outliers, void* stream);
+
+/* Dense reconstruction W[rows, cols] in `out_dtype`.
+ * Replaces triton_kernels.py:1114-1186 `dequantize_weight` (which covers only
+ * 4/8-bit; this covers 2/4/8 and the double-quantized metadata). With
+ * apply_outliers != 0 the outlier positions get base + delta, computed in
+ * fp32, as modules.py:912-919 does before its F.linear. */
+TS_API int ts_dequantize_weight(const ts_qweight* w, void* out, int out_dtype, int64_t out_row_stride,
+                         int apply_outliers, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * GPU quantize + pack (GOAP), replacing gpu_quantize.py:52-166
+ * `quantize_tensor_gpu` and the tensor work of codec.py:453-675
+ * `quantize_tensor`: top-k |w| outlier extraction and clamp, per-group affine
+ * parameters, uniform / codebook / Lloyd-Max code assignment, bit packing,
+ * double quantization of scale/gmin, and QuantLinear's row-sorted outlier
+ * tables with their fp16 deltas (modules.py:414-448, 649-715).
+ * Bit-identical to the reference codec on the same input, except that ties
+ * at the top-k threshold keep the lowest flat indices.
+ */
+typedef enum ts_qmode {
+  TS_QMODE_UNIFORM = 0,  /* round-half-even on the integer grid */
+  TS_QMODE_CODEBOOK = 1, /* nearest entry of a given sorted fp32 codebook (NF) */
+  TS_QMODE_LLOYD = 2     /* fit a Lloyd-Max codebook on the device, then assign */
+} ts_qmode;
+
+typedef struct ts_quant_params {
+  int64_t rows, cols;
+  int32_t bits, group_size;
+  int64_t k_outliers;        /* codec.py:530: max(1, int(n*frac)) or 0 */
+  int32_t double_quant;      /* 0/1 */
+  int32_t dq_group_size;
+  int32_t mode;              /* ts_qmode */
+  int32_t lloyd_iters;       /* codec.py:258 default 12 */
+  const float* codebook;     /* device fp32 [1<<bits], sorted (TS_QMODE_CODEBOOK) */
+  const int64_t* lloyd_sample; /* device flat indices into the padded
+                                  [rows, padded_cols] grid, or NULL = all */
+  int64_t lloyd_n_sample;
+} ts_quant_params;
+
+typedef struct ts_quant_outputs {
+  uint8_t* packed;           /* [rows, padded_cols*bits/8] */
+  uint16_t* scale;           /* fp16 [rows, n_groups]; DQ-reconstructed when double_quant */
+  uint16_t* gmin;
+  uint8_t* dq_scale_codes;   /* [n_super*dq_group_size] (double_quant only) */
+  uint16_t* dq_scale_meta;   /* fp16 [n_super, 2] */
+  uint8_t* dq_gmin_codes;
+  uint16_t* dq_gmin_meta;
+  float* codebook_out;       /* fp32 [1<<bits]: levels the codes were assigned
+                                against (Lloyd: the fitted levels), or NULL */
+  uint16_t* codebook_f16;    /* fp16 [1<<bits] stored codebook (Lloyd-Max: required;
+                                codebook mode: optional, and when given the
+                                outlier deltas are taken against these fp16
+                                levels, as for a companded weight), or NULL */
+  int32_t* outlier_idx;      /* [k] flat indices, ascending */
+  uint16_t* outlier_val;     /* fp16 [k] original values */
+  int32_t* outlier_row;      /* [k] row-sorted (ascending flat index order) */
+  int32_t* outlier_col;
+  uint16_t* outlier_delta;   /* fp16 [k] val - base */
+  int32_t* outlier_row_ptr;  /* [rows+1] */
+  float* threshold;          /* [1] clipping magnitude (0 when no outliers), or NULL */
+} ts_quant_outputs;
+
+TS_API size_t ts_quantize_workspace_size(const ts_quant_params* p);
+
+TS_API int ts_quantize_pack(const void* w, int w_dtype, const ts_quant_params* p,
+                     const ts_quant_outputs* o, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Lloyd-Max 1-D fit on device values, codec.py:320-361 (on a given sample):
+ * levels_out = sorted fp32 [n_levels] after `iters` Lloyd iterations started
+ * from linspace(min, max). */
+TS_API size_t ts_lloyd_fit_workspace_size(int64_t n, int n_levels);
+TS_API int ts_lloyd_fit(const float* values, int64_t n, int n_levels, int iters, float* levels_out,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Diagnostics. */
+TS_API const char* ts_last_error(void);
+TS_API const char* ts_version(void);
+/* Number of kernels this library launched on the calling thread since the
+ * last reset (bench bookkeeping). */
+TS_API int64_t ts_launch_count(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TENSORSHRINK_B200_H */

@@ -408,6 +408,37 @@ def qlinear(x: np.ndarray, q, bias: Optional[np.ndarray] = None) -> np.ndarray:
     return y.reshape(*x.shape[:-1], q.rows)
 
 
+def qlinear_rows(x: np.ndarray, q, r0: int, r1: int) -> np.ndarray:
+    """fp32 x @ W[r0:r1].T for a row block of the weight (exact outliers);
+    the chunked form of the reference's CPU forward (modules.py:924-938)."""
+    codes = unpack_codes(q.packed[r0:r1], q.bits, q.padded_cols)
+    cv = q.codebook.astype(np.float32)[codes] if getattr(q, "codebook", None) is not None \
+        else codes.astype(np.float32)
+    s, m = resolve_scale_gmin(q)
+    n = r1 - r0
+    W = (cv.reshape(n, q.n_groups, q.group_size) * s[r0:r1, :, None]
+         + m[r0:r1, :, None]).reshape(n, q.padded_cols)[:, : q.cols]
+    idx = q.outlier_idx.astype(np.int64)
+    sel = (idx >= r0 * q.cols) & (idx < r1 * q.cols)
+    if sel.any():
+        W = np.ascontiguousarray(W)
+        W.reshape(-1)[idx[sel] - r0 * q.cols] = q.outlier_val[sel].astype(np.float32)
+    return x.astype(np.float32).reshape(-1, q.cols) @ W.T
+
+
+def qlinear_threaded(x: np.ndarray, q, threads: int, chunk_rows: int = 1024,
+                     rows: Optional[int] = None) -> np.ndarray:
+    """qlinear over the first `rows` weight rows (all by default), row chunks
+    dequantized and multiplied on `threads` host threads (numpy releases the
+    GIL). Used only as the timed CPU baseline."""
+    from concurrent.futures import ThreadPoolExecutor
+    rows = q.rows if rows is None else rows
+    spans = [(r, min(r + chunk_rows, rows)) for r in range(0, rows, chunk_rows)]
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        parts = list(ex.map(lambda s: qlinear_rows(x, q, *s), spans))
+    return np.concatenate(parts, axis=-1)
+
+
 def max_rel_error(y: np.ndarray, y_ref: np.ndarray) -> float:
     """max|y - y_ref| / max|y_ref|: the GEMM tolerance metric used by tests."""
     y = np.asarray(y, dtype=np.float64)

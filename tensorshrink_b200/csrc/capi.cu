@@ -1,0 +1,222 @@
+// C ABI entry points (include/tensorshrink_b200.h): argument validation,
+// dispatch to the kernels, error reporting.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace ts {
+
+// implemented in qgemv.cu / dequant.cu / quantize.cu / qgemm_sm100.cu
+bool gemv_supported(const ts_qweight& w);
+size_t gemv_workspace_size(const ts_qweight& w);
+int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
+             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
+             void* workspace, size_t ws_bytes, cudaStream_t stream);
+int run_generic_qlinear(const ts_qweight& w, const void* x, int x_dtype, int64_t M,
+                        int64_t x_stride, const void* bias, int bias_dtype, void* out,
+                        int out_dtype, int64_t out_stride, cudaStream_t stream);
+int run_dequant(const ts_qweight& w, void* out, int out_dtype, int64_t out_stride,
+                int apply_outliers, cudaStream_t stream);
+int run_outlier_atomic(float* out, int64_t M, int64_t out_stride, const void* x, int x_dtype,
+                       int64_t x_stride, const int32_t* row, const int32_t* col,
+                       const uint16_t* delta, int64_t n, cudaStream_t stream);
+size_t quantize_ws_size(const ts_quant_params& p, int dtype);
+int run_quantize(const void* w, int dtype, const ts_quant_params& p, const ts_quant_outputs& o,
+                 char* ws, size_t ws_bytes, cudaStream_t stream);
+size_t lloyd_ws_size();
+int run_lloyd_standalone(const float* vals, int64_t n, int n_levels, int iters, float* out, char* ws,
+                         size_t ws_bytes, cudaStream_t stream);
+
+namespace {
+thread_local char g_err[1024] = "";
+thread_local int64_t g_launches = 0;
+
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+std::mutex g_dev_mu;
+std::vector<DevInfo> g_dev;
+
+const DevInfo& dev_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if ((int)g_dev.size() <= dev) g_dev.resize(dev + 1);
+  DevInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (d.sms <= 0) d.sms = 148;
+    if (d.smem_optin <= 0) d.smem_optin = 227 * 1024;
+  }
+  return d;
+}
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+void count_launch(int n) { g_launches += n; }
+int sm_count() { return dev_info().sms; }
+int max_smem_optin() { return dev_info().smem_optin; }
+
+static bool valid_act_dtype(int d) { return d == TS_F16 || d == TS_BF16; }
+static bool valid_dtype(int d) { return d == TS_F16 || d == TS_BF16 || d == TS_F32; }
+
+// Shape/pointer checks shared by every entry point taking a ts_qweight.
+static int check_qweight(const ts_qweight* w) {
+  TS_REQUIRE(w != nullptr, "qweight is NULL");
+  TS_UNSUPPORTED(w->bits == 2 || w->bits == 4 || w->bits == 8,
+                 "bits=%d not supported (2, 4 or 8)", w->bits);
+  TS_REQUIRE(w->rows >= 0 && w->cols >= 0 && w->group_size > 0, "bad weight shape");
+  TS_REQUIRE(w->padded_cols >= w->cols && w->padded_cols % w->group_size == 0 &&
+                 w->n_groups == w->padded_cols / w->group_size,
+             "inconsistent padded_cols/n_groups (cols=%lld padded=%lld gs=%d n_groups=%lld)",
+             (long long)w->cols, (long long)w->padded_cols, w->group_size, (long long)w->n_groups);
+  TS_REQUIRE(w->packed_row_bytes * 8 >= w->padded_cols * w->bits, "packed rows too short");
+  TS_REQUIRE(w->packed != nullptr || w->rows * w->cols == 0, "packed is NULL");
+  const bool plain = w->scale != nullptr && w->gmin != nullptr;
+  const bool dq = w->dq_scale_codes && w->dq_scale_meta && w->dq_gmin_codes && w->dq_gmin_meta;
+  TS_REQUIRE(plain != dq, "exactly one of scale/gmin or the four dq_* buffers must be given");
+  TS_REQUIRE(!dq || w->dq_group_size > 0, "dq_group_size must be > 0");
+  TS_REQUIRE(w->n_outliers == 0 ||
+                 ((w->outlier_row_ptr || w->outlier_row) && w->outlier_col && w->outlier_delta),
+             "outlier tables missing");
+  return TS_OK;
+}
+
+}  // namespace ts
+
+using namespace ts;
+
+extern "C" {
+
+const char* ts_last_error(void) { return g_err; }
+
+const char* ts_version(void) { return "tensorshrink_b200 0.1.0 (sm_100a)"; }
+
+int64_t ts_launch_count(int reset) {
+  const int64_t v = g_launches;
+  if (reset) g_launches = 0;
+  return v;
+}
+
+size_t ts_qlinear_workspace_size(const ts_qweight* w, int64_t M) {
+  (void)M;
+  if (!w) return 0;
+  return gemv_supported(*w) ? gemv_workspace_size(*w) : 0;
+}
+
+int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M, int64_t x_row_stride,
+               const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_row_stride,
+               void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_qweight(w);
+  if (rc != TS_OK) return rc;
+  TS_UNSUPPORTED(valid_act_dtype(x_dtype), "x dtype must be fp16 or bf16");
+  TS_UNSUPPORTED(valid_dtype(out_dtype), "out dtype must be fp16, bf16 or fp32");
+  TS_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "bad bias dtype");
+  TS_REQUIRE(M >= 0, "M < 0");
+  if (M == 0 || w->rows == 0) return TS_OK;
+  TS_REQUIRE(x != nullptr && out != nullptr, "x/out is NULL");
+  TS_REQUIRE(x_row_stride >= w->cols && out_row_stride >= w->rows, "row strides too small");
+  TS_REQUIRE(w->n_outliers == 0 || w->outlier_row_ptr != nullptr,
+             "qlinear needs the CSR outlier_row_ptr table");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (gemv_supported(*w)) {
+    TS_REQUIRE(workspace != nullptr, "workspace is NULL (size %zu needed)", gemv_workspace_size(*w));
+    return run_gemv(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
+                    out_row_stride, workspace, workspace_bytes, s);
+  }
+  return run_generic_qlinear(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
+                             out_row_stride, s);
+}
+
+int ts_apply_outlier_correction(float* out, int64_t M, int64_t N, int64_t out_row_stride,
+                                const void* x, int x_dtype, int64_t x_row_stride,
+                                const int32_t* row, const int32_t* col, const uint16_t* delta,
+                                int64_t n_outliers, void* stream) {
+  TS_UNSUPPORTED(valid_act_dtype(x_dtype) || x_dtype == TS_F32, "bad x dtype");
+  TS_REQUIRE(M >= 0 && N >= 0 && n_outliers >= 0, "negative size");
+  if (n_outliers == 0 || M == 0) return TS_OK;
+  TS_REQUIRE(out && x && row && col && delta, "NULL pointer");
+  TS_REQUIRE(out_row_stride >= N, "out stride too small");
+  return run_outlier_atomic(out, M, out_row_stride, x, x_dtype, x_row_stride, row, col, delta,
+                            n_outliers, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_dequantize_weight(const ts_qweight* w, void* out, int out_dtype, int64_t out_row_stride,
+                         int apply_outliers, void* stream) {
+  int rc = check_qweight(w);
+  if (rc != TS_OK) return rc;
+  TS_UNSUPPORTED(valid_dtype(out_dtype), "out dtype must be fp16, bf16 or fp32");
+  TS_REQUIRE(out != nullptr || w->rows * w->cols == 0, "out is NULL");
+  TS_REQUIRE(out_row_stride >= w->cols, "out stride too small");
+  TS_REQUIRE(!apply_outliers || w->n_outliers == 0 || w->outlier_row != nullptr,
+             "outlier_row needed to apply outliers");
+  return run_dequant(*w, out, out_dtype, out_row_stride, apply_outliers,
+                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+static int check_qparams(const ts_quant_params* p) {
+  TS_REQUIRE(p != nullptr, "params is NULL");
+  TS_UNSUPPORTED(p->bits == 2 || p->bits == 4 || p->bits == 8, "bits=%d not supported", p->bits);
+  const int gs = p->group_size;
+  TS_UNSUPPORTED(gs >= 8 && gs <= 256 && (gs & (gs - 1)) == 0,
+                 "group_size=%d not supported by the GPU quantizer (power of two in [8, 256])", gs);
+  TS_REQUIRE(p->rows > 0 && p->cols > 0, "empty weight");
+  TS_REQUIRE(p->rows * p->cols < (1ll << 31), "weight too large for int32 outlier indices");
+  TS_REQUIRE(p->k_outliers >= 0, "k_outliers < 0");
+  TS_REQUIRE(!p->double_quant || p->dq_group_size > 0, "dq_group_size must be > 0");
+  TS_REQUIRE(p->mode >= 0 && p->mode <= 2, "bad mode");
+  TS_REQUIRE(p->mode != TS_QMODE_LLOYD || (p->lloyd_iters >= 0), "bad lloyd_iters");
+  return TS_OK;
+}
+
+size_t ts_quantize_workspace_size(const ts_quant_params* p) {
+  if (!p) return 0;
+  // sized for the widest key (fp32 input)
+  return quantize_ws_size(*p, TS_F32);
+}
+
+int ts_quantize_pack(const void* w, int w_dtype, const ts_quant_params* p, const ts_quant_outputs* o,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_qparams(p);
+  if (rc != TS_OK) return rc;
+  TS_UNSUPPORTED(valid_dtype(w_dtype), "weight dtype must be fp16, bf16 or fp32");
+  TS_REQUIRE(w && o && o->packed && o->scale && o->gmin && o->outlier_row_ptr, "NULL pointer");
+  const bool outl = p->k_outliers > 0 && p->k_outliers < p->rows * p->cols;
+  TS_REQUIRE(!outl || (o->outlier_idx && o->outlier_val && o->outlier_row && o->outlier_col &&
+                       o->outlier_delta),
+             "outlier outputs missing");
+  TS_REQUIRE(!p->double_quant || (o->dq_scale_codes && o->dq_scale_meta && o->dq_gmin_codes &&
+                                  o->dq_gmin_meta),
+             "double-quant outputs missing");
+  TS_REQUIRE(is_aligned(o->packed, 8), "packed output must be 8-byte aligned");
+  TS_REQUIRE(workspace != nullptr, "workspace is NULL");
+  return run_quantize(w, w_dtype, *p, *o, reinterpret_cast<char*>(workspace), workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ts_lloyd_fit_workspace_size(int64_t n, int n_levels) {
+  (void)n;
+  (void)n_levels;
+  return lloyd_ws_size();
+}
+
+int ts_lloyd_fit(const float* values, int64_t n, int n_levels, int iters, float* levels_out,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  TS_REQUIRE(values && levels_out && workspace, "NULL pointer");
+  return run_lloyd_standalone(values, n, n_levels, iters, levels_out,
+                              reinterpret_cast<char*>(workspace), workspace_bytes,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
