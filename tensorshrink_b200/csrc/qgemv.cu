@@ -61,7 +61,10 @@ struct Args {
   uint32_t chunks;     // 512-byte chunks per row
   uint32_t total_warps;
   int n_chunks_x;      // chunks covering padded_cols (activation staging)
-  float center;        // C in the identity above
+  int x_vec16;         // rows of x are 16-byte aligned (vector staging loads)
+  int gbytes_shift;    // log2(bytes of packed codes per group)
+  int dq_shift;        // log2(dq_group_size) when a power of two, else -1
+  float center;        // C in the identity above (uniform grids; codebooks use their midpoint)
 };
 
 // Position of weight offset j (0..WORD_W-1) inside the fp16 activation block
@@ -186,11 +189,10 @@ struct MetaRaw {
 };
 
 template <bool DQ>
-__device__ __forceinline__ MetaRaw load_meta(const QW& q, int64_t row, int64_t g) {
+__device__ __forceinline__ MetaRaw load_meta(const QW& q, uint32_t flat, int dq_shift) {
   MetaRaw m;
-  const int64_t flat = row * q.n_groups + g;
   if constexpr (DQ) {
-    const int64_t sup = flat / q.dq_gs;
+    const uint32_t sup = dq_shift >= 0 ? (flat >> dq_shift) : flat / (uint32_t)q.dq_gs;
     m.a = (uint32_t)__ldg(q.dqs_codes + flat) | ((uint32_t)__ldg(q.dqg_codes + flat) << 8);
     m.b = h22u(__ldg(q.dqs_meta + sup));
     m.c = h22u(__ldg(q.dqg_meta + sup));
@@ -220,23 +222,34 @@ struct Stage {
   MetaRaw m[kR];
 };
 
+// Unit position (row group, 512-byte chunk), advanced incrementally so the
+// streaming loop does no integer division.
+struct Cursor {
+  uint32_t rg, ch;
+};
+
 template <int BITS, bool DQ>
-__device__ __forceinline__ void load_stage(Stage& st, const Args& a, uint32_t u, int lane) {
-  const uint32_t rg = u / a.chunks;
-  const uint32_t ch = u - rg * a.chunks;
-  const int64_t boff = (int64_t)ch * 512 + lane * 16;
-  const int64_t gbytes = (int64_t)a.q.group_size * BITS / 8;
-  const bool valid = boff < a.q.row_bytes;
+__device__ __forceinline__ void load_stage(Stage& st, const Args& a, const Cursor c, int lane) {
+  const uint32_t boff = c.ch * 512u + lane * 16u;
+  const bool valid = boff < (uint32_t)a.q.row_bytes;
+  const uint32_t g = boff >> a.gbytes_shift;
 #pragma unroll
   for (int r = 0; r < kR; ++r) {
-    const int64_t row = (int64_t)rg * kR + r;
-    if (valid && row < a.q.rows) {
-      st.w[r] = ldg_stream_v4(a.q.packed + row * a.q.row_bytes + boff);
-      st.m[r] = load_meta<DQ>(a.q, row, boff / gbytes);
+    const uint32_t row = c.rg * kR + r;
+    if (valid && row < (uint32_t)a.q.rows) {
+      st.w[r] = ldg_stream_v4(a.q.packed + (size_t)row * (size_t)a.q.row_bytes + boff);
+      st.m[r] = load_meta<DQ>(a.q, row * (uint32_t)a.q.n_groups + g, a.dq_shift);
     } else {
       st.w[r] = make_uint4(0, 0, 0, 0);
       st.m[r] = MetaRaw{0, 0, 0};
     }
+  }
+}
+
+__device__ __forceinline__ void advance(Cursor& c, uint32_t chunks) {
+  if (++c.ch == chunks) {
+    c.ch = 0;
+    ++c.rg;
   }
 }
 
@@ -277,7 +290,7 @@ __device__ void finish_rows(const Args& a, uint32_t rg, float (&tot)[kR][MT], in
 }
 
 template <int BITS, bool CB, bool DQ, int MT>
-__global__ void __launch_bounds__(kThreads) qgemv_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const Args a) {
   using G = Geo<BITS>;
   extern __shared__ __align__(16) char smem[];
   constexpr int LUT_BYTES = !CB ? 0 : (BITS == 2 ? 256 * 32 * 8 : 256 * 32 * 4);
@@ -297,61 +310,104 @@ __global__ void __launch_bounds__(kThreads) qgemv_kernel(const Args a) {
   // 1. Start streaming this warp's first weights (independent of x).
   constexpr int D = 3;
   Stage st[D];
+  const uint32_t first_rg = u_begin / a.chunks;
+  Cursor pf{first_rg, u_begin - first_rg * a.chunks};  // prefetch cursor
 #pragma unroll
   for (int d = 0; d < D; ++d)
-    if (u_begin + d < u_end) load_stage<BITS, DQ>(st[d], a, u_begin + d, lane);
+    if (u_begin + d < u_end) {
+      load_stage<BITS, DQ>(st[d], a, pf, lane);
+      advance(pf, a.chunks);
+    }
 
   // 2. Codebook lookup table (per-lane copies: conflict-free random access).
+  //    Centre C = midpoint of the codebook range keeps the fp16 levels small.
+  float center = a.center;
   if constexpr (CB) {
-    const int levels = 1 << BITS;
+    const float* cb = a.q.codebook;
+    center = 0.5f * (__ldg(cb) + __ldg(cb + (1 << BITS) - 1));
     for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
       const int b = i >> 5, l = i & 31;
       if constexpr (BITS == 4) {
-        const half2 v = __floats2half2_rn(a.q.codebook[b & 15] - a.center, a.q.codebook[b >> 4] - a.center);
+        const half2 v = __floats2half2_rn(__ldg(cb + (b & 15)) - center, __ldg(cb + (b >> 4)) - center);
         reinterpret_cast<uint32_t*>(lut)[b * 32 + l] = h22u(v);
       } else if constexpr (BITS == 2) {
-        const half2 v0 = __floats2half2_rn(a.q.codebook[b & 3] - a.center, a.q.codebook[(b >> 2) & 3] - a.center);
-        const half2 v1 = __floats2half2_rn(a.q.codebook[(b >> 4) & 3] - a.center, a.q.codebook[b >> 6] - a.center);
+        const half2 v0 = __floats2half2_rn(__ldg(cb + (b & 3)) - center, __ldg(cb + ((b >> 2) & 3)) - center);
+        const half2 v1 = __floats2half2_rn(__ldg(cb + ((b >> 4) & 3)) - center, __ldg(cb + (b >> 6)) - center);
         reinterpret_cast<uint2*>(lut)[b * 32 + l] = make_uint2(h22u(v0), h22u(v1));
       } else {
-        (void)levels;
-        reinterpret_cast<uint32_t*>(lut)[b * 32 + l] = f2h(a.q.codebook[b] - a.center);
+        reinterpret_cast<uint32_t*>(lut)[b * 32 + l] = f2h(__ldg(cb + b) - center);
       }
     }
   }
 
-  // 3. Wait for the producer of x (programmatic dependent launch), stage it.
+  // 3. Wait for the producer of x (programmatic dependent launch), stage it:
+  //    one thread per 8 consecutive activations; the SPAN/8 threads of a span
+  //    (an aligned lane group) reduce its max |x| and sum with shuffles.
   pdl_wait_primary();
-  for (int i = threadIdx.x; i < MT * n_spans; i += kThreads) {
-    const int m = i / n_spans, s = i - m * n_spans;
-    const int64_t k0 = (int64_t)s * G::SPAN;
-    const bool tok = m < a.mt;
-    const int64_t xoff = (a.m0 + m) * a.x_stride;
-    float mx = 0.f, sum = 0.f;
-    for (int j = 0; j < G::SPAN; ++j) {
-      const int64_t k = k0 + j;
-      const float v = (tok && k < a.q.cols) ? load_f(a.x, a.x_dtype, xoff + k) : 0.f;
-      mx = fmaxf(mx, fabsf(v));
-      sum += v;
-    }
-    int e = 0;
-    if (mx > 0.f) frexpf(mx, &e);
-    sx[m * n_spans + s] = make_float2(ldexpf(1.f, e), sum);
-    const int ch = s >> 5, l = s & 31;
-    __half* dst = xs + m * x_tok + (int64_t)ch * G::CHUNK_W;
-    for (int j = 0; j < G::SPAN; ++j) {
-      const int64_t k = k0 + j;
-      const float v = (tok && k < a.q.cols) ? load_f(a.x, a.x_dtype, xoff + k) : 0.f;
-      const int word = j / G::WORD_W, jj = j - word * G::WORD_W;
-      const int o = word * G::WORD_W + word_pos<BITS, CB>(jj);
-      dst[((o >> 3) * 32 + l) * 8 + (o & 7)] = __float2half_rn(ldexpf(v, -e));
+  {
+    constexpr int TPS = G::SPAN / 8;
+    const uint32_t per_tok = (uint32_t)(a.q.padded_cols / 8);
+    const uint32_t items = MT * per_tok;
+    for (uint32_t base = 0; base < items; base += kThreads) {
+      const uint32_t it = base + threadIdx.x;
+      const bool live = it < items;
+      const uint32_t m = live ? it / per_tok : 0;
+      const uint32_t k0 = live ? (it - m * per_tok) * 8 : 0;
+      const bool tok = live && (int)m < a.mt;
+      const int64_t xoff = (a.m0 + m) * a.x_stride + k0;
+      float v[8];
+      if (tok && a.x_vec16 && k0 + 8 <= (uint32_t)a.q.cols) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + xoff));
+        const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (a.x_dtype == TS_F16) {
+            const float2 f = __half22float2(u2h2(r4[j]));
+            v[2 * j] = f.x;
+            v[2 * j + 1] = f.y;
+          } else {
+            v[2 * j] = __uint_as_float(r4[j] << 16);
+            v[2 * j + 1] = __uint_as_float(r4[j] & 0xFFFF0000u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[j] = (tok && k0 + j < (uint32_t)a.q.cols) ? load_f(a.x, a.x_dtype, xoff + j) : 0.f;
+      }
+      float mx = 0.f, sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        mx = fmaxf(mx, fabsf(v[j]));
+        sum += v[j];
+      }
+#pragma unroll
+      for (int o = TPS / 2; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      }
+      int e = 0;
+      if (mx > 0.f) frexpf(mx, &e);
+      if (live) {
+        const uint32_t sp = k0 / G::SPAN;          // span index within the token
+        const int j0 = (int)(k0 - sp * G::SPAN);   // this thread's offset in the span
+        if (j0 == 0) sx[m * n_spans + sp] = make_float2(ldexpf(1.f, e), sum);
+        __half* dst = xs + m * x_tok + (int64_t)(sp >> 5) * G::CHUNK_W;
+        const int l = (int)(sp & 31);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int jj = j0 + j;
+          const int word = jj / G::WORD_W, jw = jj - word * G::WORD_W;
+          const int o = word * G::WORD_W + word_pos<BITS, CB>(jw);
+          dst[((o >> 3) * 32 + l) * 8 + (o & 7)] = __float2half_rn(ldexpf(v[j], -e));
+        }
+      }
     }
   }
   __syncthreads();
   pdl_launch_dependents();
 
   if (u_begin >= u_end) return;
-  const uint32_t first_rg = u_begin / a.chunks;
   const char* lut_lane = lut + lane * (BITS == 2 ? 8 : 4);
 
   float acc[kR][MT];
@@ -363,7 +419,6 @@ __global__ void __launch_bounds__(kThreads) qgemv_kernel(const Args a) {
   uint32_t rg = first_rg;
   uint32_t ch = u_begin - rg * a.chunks;
   bool started_here = ch == 0;
-  const int64_t gbytes = (int64_t)a.q.group_size * BITS / 8;
 
   for (uint32_t base = u_begin; base < u_end; base += D) {
 #pragma unroll
@@ -371,38 +426,40 @@ __global__ void __launch_bounds__(kThreads) qgemv_kernel(const Args a) {
       const uint32_t u = base + d;
       if (u < u_end) {
         const Stage cur = st[d];
-        if (u + D < u_end) load_stage<BITS, DQ>(st[d], a, u + D, lane);
-        const int64_t boff = (int64_t)ch * 512 + lane * 16;
-        if (boff < a.q.row_bytes) {
-          const int s = ch * 32 + lane;
+        if (u + D < u_end) {
+          load_stage<BITS, DQ>(st[d], a, pf, lane);
+          advance(pf, a.chunks);
+        }
+        const uint32_t boff = ch * 512u + lane * 16u;
+        if (boff < (uint32_t)a.q.row_bytes) {
+          const uint32_t sp = ch * 32 + lane;
           float2 fx[MT];
 #pragma unroll
-          for (int m = 0; m < MT; ++m) fx[m] = sx[m * n_spans + s];
+          for (int m = 0; m < MT; ++m) fx[m] = sx[m * n_spans + sp];
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
             if (m < a.mt) {
               const uint4* xv = reinterpret_cast<const uint4*>(xs + m * x_tok + (int64_t)ch * G::CHUNK_W) + lane;
-              // xv[v] must step over the 32 lanes: vector v of this lane sits at +v*32.
-              uint4 xl[G::VEC];
+              uint4 xl[G::VEC];  // vector v of this lane sits v*32 uint4s further
 #pragma unroll
               for (int v = 0; v < G::VEC; ++v) xl[v] = xv[v * 32];
 #pragma unroll
               for (int r = 0; r < kR; ++r) {
                 const uint32_t wq[4] = {cur.w[r].x, cur.w[r].y, cur.w[r].z, cur.w[r].w};
-                float p = 0.f;
+                float p0 = 0.f, p1 = 0.f;
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
                   const float2 f2 = __half22float2(word_dot<BITS, CB>(wq[w], xl, w, lut_lane));
-                  p += f2.x + f2.y;
+                  p0 += f2.x;
+                  p1 += f2.y;
                 }
                 const float2 sg = decode_meta<DQ>(cur.m[r]);
-                const float gprime = fmaf(a.center, sg.x, sg.y);
-                acc[r][m] = fmaf(sg.x * fx[m].x, p, fmaf(gprime, fx[m].y, acc[r][m]));
+                const float gprime = fmaf(center, sg.x, sg.y);
+                acc[r][m] = fmaf(sg.x * fx[m].x, p0 + p1, fmaf(gprime, fx[m].y, acc[r][m]));
               }
             }
           }
         }
-        (void)gbytes;
         const bool last_chunk = ch == a.chunks - 1;
         if (last_chunk || u == u_end - 1) {
           // ---- flush this row group ----
@@ -429,16 +486,24 @@ __global__ void __launch_bounds__(kThreads) qgemv_kernel(const Args a) {
             int old = 0;
             if (lane == 0) old = atomicAdd(a.counters + rg, 1);
             old = __shfl_sync(0xffffffffu, old, 0);
+            // pieces = distinct non-empty warps owning this row group's units
             const uint64_t u0 = (uint64_t)rg * a.chunks;
-            const uint32_t wf = warp_of(u0, U, W);
-            const uint32_t wl = warp_of(u0 + a.chunks - 1, U, W);
-            if (old == (int)(wl - wf)) {
+            int pieces = 1;
+            for (uint32_t c = 1, prev = warp_of(u0, U, W); c < a.chunks; ++c) {
+              const uint32_t w = warp_of(u0 + c, U, W);
+              pieces += w != prev;
+              prev = w;
+            }
+            if (old == pieces - 1) {
               __threadfence();
 #pragma unroll
               for (int r = 0; r < kR; ++r)
 #pragma unroll
                 for (int m = 0; m < MT; ++m) tot[r][m] = 0.f;
-              for (uint32_t pw = wf; pw <= wl; ++pw) {
+              for (uint32_t c = 0, prev = 0xFFFFFFFFu; c < a.chunks; ++c) {
+                const uint32_t pw = warp_of(u0 + c, U, W);
+                if (pw == prev) continue;
+                prev = pw;
                 const uint32_t pfirst = (uint32_t)((U * pw / W) / a.chunks);
                 const float* src = a.partials + ((size_t)pw * 2 + (rg == pfirst ? 0 : 1)) * (kR * MT);
 #pragma unroll
@@ -503,8 +568,7 @@ template <int BITS, bool CB, bool DQ>
 int launch_mt(int mt, const gemv::Args& a, cudaStream_t s, size_t smem) {
   if (mt <= 1) return launch_one<BITS, CB, DQ, 1>(a, 0, s, smem);
   if (mt <= 2) return launch_one<BITS, CB, DQ, 2>(a, 0, s, smem);
-  if (mt <= 4) return launch_one<BITS, CB, DQ, 4>(a, 0, s, smem);
-  return launch_one<BITS, CB, DQ, 8>(a, 0, s, smem);
+  return launch_one<BITS, CB, DQ, 4>(a, 0, s, smem);
 }
 
 template <int BITS>
@@ -514,15 +578,23 @@ int launch_bits(bool cb, bool dq, int mt, const gemv::Args& a, cudaStream_t s, s
 }
 
 int pick_mt(int64_t tokens) {
-  return tokens <= 1 ? 1 : tokens <= 2 ? 2 : tokens <= 4 ? 4 : 8;
+  return tokens <= 1 ? 1 : tokens <= 2 ? 2 : 4;
 }
 
 }  // namespace
 
+static int ilog2(int64_t v) {
+  int r = 0;
+  while ((int64_t(1) << (r + 1)) <= v) ++r;
+  return r;
+}
+
 // Whether the fast GEMV covers this weight layout.
 bool gemv_supported(const ts_qweight& w) {
-  const int span_bytes_group = w.group_size * w.bits / 8;
-  return (w.bits == 2 || w.bits == 4 || w.bits == 8) && span_bytes_group % 16 == 0 &&
+  const int64_t gbytes = (int64_t)w.group_size * w.bits / 8;
+  return (w.bits == 2 || w.bits == 4 || w.bits == 8) && gbytes % 16 == 0 &&
+         (gbytes & (gbytes - 1)) == 0 && w.rows * w.n_groups < (int64_t(1) << 31) &&
+         w.packed_row_bytes < (int64_t(1) << 30) &&
          w.packed_row_bytes % 16 == 0 && is_aligned(w.packed, 16) &&
          w.padded_cols % (128 / w.bits) == 0 && w.packed_row_bytes * 8 / w.bits >= w.padded_cols;
 }
@@ -532,7 +604,7 @@ static int gemv_grid_warps() { return sm_count() * 2 * gemv::kWarps; }
 size_t gemv_workspace_size(const ts_qweight& w) {
   const int64_t rgs = (w.rows + gemv::kR - 1) / gemv::kR;
   return align_up((size_t)rgs * sizeof(int), 256) +
-         (size_t)gemv_grid_warps() * 2 * gemv::kR * 8 * sizeof(float);
+         (size_t)gemv_grid_warps() * 2 * gemv::kR * 4 * sizeof(float);
 }
 
 static size_t gemv_smem(const ts_qweight& w, int mt) {
@@ -546,7 +618,7 @@ static size_t gemv_smem(const ts_qweight& w, int mt) {
 // Largest token count per pass whose staged activations fit in shared memory.
 int gemv_max_tokens(const ts_qweight& w) {
   const size_t cap = (size_t)std::min(max_smem_optin(), 200 * 1024);
-  for (int mt : {8, 4, 2, 1})
+  for (int mt : {4, 2, 1})
     if (gemv_smem(w, mt) <= cap) return mt;
   return 0;
 }
@@ -578,13 +650,11 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.total_warps = (uint32_t)gemv_grid_warps();
   const int64_t chunk_w = 32 * (128 / w.bits);
   a.n_chunks_x = (int)((w.padded_cols + chunk_w - 1) / chunk_w);
-  if (w.codebook) {
-    // centre of the codebook range; computed on the host from a device copy
-    // would need a sync, so the kernel takes it from the caller-side cache.
-    a.center = 0.f;
-  } else {
-    a.center = w.bits == 4 ? 8.f : w.bits == 2 ? 2.f : 128.f;
-  }
+  a.center = w.bits == 4 ? 8.f : w.bits == 2 ? 2.f : 128.f;  // codebooks: set in-kernel
+  a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0;
+  a.gbytes_shift = ilog2((int64_t)w.group_size * w.bits / 8);
+  a.dq_shift = (w.dq_scale_codes && (w.dq_group_size & (w.dq_group_size - 1)) == 0)
+                   ? ilog2(w.dq_group_size) : -1;
   for (int64_t m0 = 0; m0 < M; m0 += max_mt) {
     const int64_t tokens = std::min<int64_t>(max_mt, M - m0);
     const int mt = pick_mt(tokens);
