@@ -1,331 +1,339 @@
-// Decode-shaped fused dequant-GEMV (M <= 8 tokens per pass) on CUDA cores.
+// Decode-shaped fused dequant-GEMV (up to 8 tokens per pass) for sm_100a.
 //
 // Replaces the reference's `_fused_dequant_matmul_{2,4,8}bit` Triton kernels
 // (tensorshrink triton_kernels.py:278-541) for decode shapes, with the
 // outlier correction of `_add_outlier_tile` / `_outlier_correction_kernel`
-// (triton_kernels.py:154-232, 543-576) folded into the row epilogue.
+// (triton_kernels.py:154-232, 543-576) and the bias folded into the epilogue.
 //
-// Work decomposition. The packed matrix is cut into "units": R consecutive
-// rows x one 512-byte chunk of each row. A warp processes a unit with one
-// 16-byte streaming load per lane per row (LDG.128, L1 bypassed), so a lane
-// always covers exactly one 16-byte span of one quantization group. Units are
-// numbered row-group-major and every warp of the persistent grid takes an
-// equal contiguous range, so HBM traffic is balanced to within one unit. Rows
-// wholly inside one warp's range are finished by that warp; a row split
-// between warps is finished by whichever piece arrives last (per-row counter
-// in the workspace), which sums the pieces' partials in warp order, so the
-// result is deterministic.
+// Streaming. The packed matrix is cut into tiles of 16 rows x 2 KB. Each
+// persistent CTA owns an equal contiguous range of tiles (row-block major), so
+// HBM traffic is balanced to within one tile. A producer warp streams each
+// tile row with a 1-D bulk copy (16 lanes, one row each) and the tile's
+// group metadata with 4-byte async copies into a ring of shared-memory stages
+// guarded by mbarriers (full: all bytes landed; empty: consumers done), so
+// the bytes in flight do not depend on how fast the math runs. Rows are
+// stored with a 2064-byte pitch, which makes the fragment reads below
+// bank-conflict-free.
 //
-// Arithmetic. Per (row, group) the reconstruction is w = v(code)*s + g, so
-//   sum_k x_k w_k = s * sum_k x_k (v_k - C) + (g + C*s) * sum_k x_k
-// with a centring constant C. The activations are staged once per CTA in
-// shared memory as fp16 scaled by a power of two per 16-byte span (exact
-// rescale, keeps every partial product in fp16 range), together with the
-// span's fp32 sum. Codes are turned into fp16 (v - C) values either with the
-// exponent-bias trick (uniform grids: integer codes OR-ed into the mantissa
-// of 1024.0) or through a per-lane-replicated byte lookup table in shared
-// memory (NF / Lloyd-Max codebooks); products are accumulated with HFMA2 over
-// one 32-bit word of codes and then in fp32.
+// Math. Consumer warp w owns the 128-byte slice [128w, 128w+128) of every
+// tile row: 8 chunks of 16 bytes, each one m16 x k tensor-core step. Lane
+// (q, l) = (lane/4, lane%4) holds rows q and q+8 and reads the 4-byte word at
+// 4l of a chunk, so the k of every MMA come from one chunk and hence one
+// quantization group. Codes become fp16 (v - C) values in registers (uniform
+// grids: the exponent-bias trick, integer codes OR-ed into the mantissa of
+// 1024.0; NF / Lloyd-Max codebooks: a per-lane byte lookup table in shared
+// memory) and feed mma.sync m16n8k16 with fp32 accumulation; the 8 columns
+// are the (up to 8) tokens. The k order inside an MMA is free, so the
+// activations (B) are staged in exactly the order the code words unpack. Per
+// (row, group) the reconstruction is w = v*s + g, so
+//   sum_k x_k w_k = s * sum_k x_k (v_k - C) + (g + C*s) * sum_k x_k ,
+// applied once per group segment with the segment's fp32 activation sum. The
+// activations are staged as fp16 scaled by a power of two per segment (exact
+// rescale into [-1, 1]).
+//
+// Row blocks wholly inside one CTA's range are finished by that CTA; a row
+// block split between CTAs is finished by whichever CTA arrives last (per
+// row-block counter in the workspace), which sums the pieces' partials in CTA
+// order, so results are deterministic. The outlier correction
+// (x[:, col] * delta over the CSR row slice) and the bias of every row block
+// whose first tile a CTA owns are computed in the prologue while the
+// producer fills the first stages.
+#include <mutex>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace ts {
 namespace gemv {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kR = 2;  // rows per unit
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
+constexpr int kTileRows = 16;
+constexpr int kTileK = 2048;                       // packed bytes per row per tile
+constexpr int kSlice = kTileK / kConsumerWarps;    // 128 bytes per warp per row
+constexpr int kPitch = kTileK + 16;                // smem row pitch (conflict-free)
+constexpr int kMaxStages = 6;
+constexpr int kMaxTok = 8;
+constexpr int kMaxSupers = 64;                     // double-quant super-groups per tile
+constexpr int kOutCap = 2048;                      // outliers preloaded per CTA (more: read in place)
+constexpr int kCbuf = 2048;                        // outlier contributions per epilogue pass
 
 template <int BITS>
 struct Geo {
-  static constexpr int SPAN = 128 / BITS;      // weights per lane per unit (16 bytes)
-  static constexpr int VEC = SPAN / 8;         // 16-byte fp16 activation vectors per span
-  static constexpr int WORD_W = 32 / BITS;     // weights per 32-bit word of codes
-  static constexpr int CHUNK_W = 32 * SPAN;    // weights per 512-byte chunk
+  static constexpr int PPW = 16 / BITS;       // fp16 pairs per 32-bit code word
+  static constexpr int MPW = PPW / 2;         // MMAs per word (per 16-byte chunk)
+  static constexpr int KPW = 32 / BITS;       // codes per word
+  static constexpr int KPC = 128 / BITS;      // codes per 16-byte chunk
 };
-
-struct Args {
-  QW q;
-  const void* x;
-  int x_dtype;
-  int64_t x_stride;
-  int64_t m0;      // first token of this pass
-  int mt;          // tokens in this pass (<= MT)
-  const void* bias;
-  int bias_dtype;
-  void* out;
-  int out_dtype;
-  int64_t out_stride;
-  float* partials;
-  int* counters;
-  uint32_t units;      // n_rowgroups * chunks
-  uint32_t chunks;     // 512-byte chunks per row
-  uint32_t total_warps;
-  int n_chunks_x;      // chunks covering padded_cols (activation staging)
-  int x_vec16;         // rows of x are 16-byte aligned (vector staging loads)
-  int gbytes_shift;    // log2(bytes of packed codes per group)
-  int dq_shift;        // log2(dq_group_size) when a power of two, else -1
-  float center;        // C in the identity above (uniform grids; codebooks use their midpoint)
-};
-
-// Position of weight offset j (0..WORD_W-1) inside the fp16 activation block
-// that matches the order in which codes come out of a 32-bit word.
-template <int BITS, bool CB>
-__device__ __forceinline__ int word_pos(int j) {
-  if (CB || BITS == 8) return j;
-  constexpr int H = Geo<BITS>::WORD_W / 2;  // the trick yields pairs (j, j+H)
-  return j < H ? 2 * j : 2 * (j - H) + 1;
-}
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));  // (a & b) | c
   return r;
 }
-
 __device__ __forceinline__ half2 u2h2(uint32_t v) { return *reinterpret_cast<half2*>(&v); }
 __device__ __forceinline__ uint32_t h22u(half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ uint32_t hsub(uint32_t a, uint32_t b) { return h22u(__hsub2(u2h2(a), u2h2(b))); }
+__device__ __forceinline__ uint32_t hfma(uint32_t a, uint32_t b, uint32_t c) {
+  return h22u(__hfma2(u2h2(a), u2h2(b), u2h2(c)));
+}
 
-// One 32-bit word of codes dotted with its activations; returns the half2
-// partial (lanes of the pair summed later in fp32). `xv` points at the span's
-// fp16 activation vectors (uint4 = 8 halves).
+// Offsets (within the word's codes) of the two codes that pair p holds.
 template <int BITS, bool CB>
-__device__ __forceinline__ half2 word_dot(uint32_t q, const uint4* xv, int w, const char* lut) {
+__host__ __device__ __forceinline__ int2 pair_off(int p) {
+  if (!CB && BITS == 4) return make_int2(p, p + 4);
+  if (!CB && BITS == 2) return make_int2(p, p + 8);
+  return make_int2(2 * p, 2 * p + 1);
+}
+
+// Code multiplier m of pair p in the raw uniform-grid unpacking (the pair
+// holds 1024 + m*code); codebook lookups hold v - C directly (m = 1).
+template <int BITS, bool CB>
+__host__ __device__ __forceinline__ float pair_mult(int p) {
+  if (!CB && BITS == 4) return (p & 1) ? 16.f : 1.f;
+  if (!CB && BITS == 2) return (float)(1 << (2 * (p & 3)));
+  return 1.f;
+}
+
+// Unpack one 32-bit word of codes into PPW fp16 pairs, in the order
+// the MMAs consume them. `lut` points at this lane's lookup-table column.
+template <int BITS, bool CB>
+__device__ __forceinline__ void expand(uint32_t q, const char* lut, uint32_t (&P)[Geo<BITS>::PPW]) {
   if constexpr (!CB && BITS == 4) {
-    // (1024 + n) with n at the low nibble of each 16-bit half; then /16 for
-    // the nibble sitting at bits 4-7. Centre C = 8.
-    const uint4 xa = xv[w];
-    const uint32_t t0 = lop_and_or(q, 0x000F000Fu, 0x64006400u);
-    const uint32_t t1 = lop_and_or(q, 0x00F000F0u, 0x64006400u);
+    // (1024 + m*n) with m = 1 (pairs 0, 2) or 16 (pairs 1, 3); the 1024 and
+    // the m are removed on the activation side (see pair_mult)
     const uint32_t q2 = q >> 8;
-    const uint32_t t2 = lop_and_or(q2, 0x000F000Fu, 0x64006400u);
-    const uint32_t t3 = lop_and_or(q2, 0x00F000F0u, 0x64006400u);
-    const half2 c0 = __hsub2(u2h2(t0), u2h2(0x64086408u));                      // n - 8
-    const half2 c1 = __hfma2(u2h2(t1), u2h2(0x2C002C00u), u2h2(0xD480D480u));   // (1024+16n)/16 - 72
-    const half2 c2 = __hsub2(u2h2(t2), u2h2(0x64086408u));
-    const half2 c3 = __hfma2(u2h2(t3), u2h2(0x2C002C00u), u2h2(0xD480D480u));
-    half2 a = __hmul2(c0, u2h2(xa.x));
-    a = __hfma2(c1, u2h2(xa.y), a);
-    a = __hfma2(c2, u2h2(xa.z), a);
-    a = __hfma2(c3, u2h2(xa.w), a);
-    return a;
+    P[0] = lop_and_or(q, 0x000F000Fu, 0x64006400u);
+    P[1] = lop_and_or(q, 0x00F000F0u, 0x64006400u);
+    P[2] = lop_and_or(q2, 0x000F000Fu, 0x64006400u);
+    P[3] = lop_and_or(q2, 0x00F000F0u, 0x64006400u);
   } else if constexpr (!CB && BITS == 2) {
-    // 16 crumbs: pairs (j, j+8); crumb at bits 2i of each half scaled by 4^-i.
-    const uint4 xa = xv[2 * w];
-    const uint4 xb = xv[2 * w + 1];
+    // (1024 + m*n) with m = 1, 4, 16, 64 by crumb position
     const uint32_t q2 = q >> 8;
-    const half2 c0 = __hsub2(u2h2(lop_and_or(q, 0x00030003u, 0x64006400u)), u2h2(0x64026402u));
-    const half2 c1 = __hfma2(u2h2(lop_and_or(q, 0x000C000Cu, 0x64006400u)), u2h2(0x34003400u), u2h2(0xDC08DC08u));
-    const half2 c2 = __hfma2(u2h2(lop_and_or(q, 0x00300030u, 0x64006400u)), u2h2(0x2C002C00u), u2h2(0xD420D420u));
-    const half2 c3 = __hfma2(u2h2(lop_and_or(q, 0x00C000C0u, 0x64006400u)), u2h2(0x24002400u), u2h2(0xCC80CC80u));
-    const half2 c4 = __hsub2(u2h2(lop_and_or(q2, 0x00030003u, 0x64006400u)), u2h2(0x64026402u));
-    const half2 c5 = __hfma2(u2h2(lop_and_or(q2, 0x000C000Cu, 0x64006400u)), u2h2(0x34003400u), u2h2(0xDC08DC08u));
-    const half2 c6 = __hfma2(u2h2(lop_and_or(q2, 0x00300030u, 0x64006400u)), u2h2(0x2C002C00u), u2h2(0xD420D420u));
-    const half2 c7 = __hfma2(u2h2(lop_and_or(q2, 0x00C000C0u, 0x64006400u)), u2h2(0x24002400u), u2h2(0xCC80CC80u));
-    half2 a = __hmul2(c0, u2h2(xa.x));
-    a = __hfma2(c1, u2h2(xa.y), a);
-    a = __hfma2(c2, u2h2(xa.z), a);
-    a = __hfma2(c3, u2h2(xa.w), a);
-    a = __hfma2(c4, u2h2(xb.x), a);
-    a = __hfma2(c5, u2h2(xb.y), a);
-    a = __hfma2(c6, u2h2(xb.z), a);
-    a = __hfma2(c7, u2h2(xb.w), a);
-    return a;
+    P[0] = lop_and_or(q, 0x00030003u, 0x64006400u);
+    P[1] = lop_and_or(q, 0x000C000Cu, 0x64006400u);
+    P[2] = lop_and_or(q, 0x00300030u, 0x64006400u);
+    P[3] = lop_and_or(q, 0x00C000C0u, 0x64006400u);
+    P[4] = lop_and_or(q2, 0x00030003u, 0x64006400u);
+    P[5] = lop_and_or(q2, 0x000C000Cu, 0x64006400u);
+    P[6] = lop_and_or(q2, 0x00300030u, 0x64006400u);
+    P[7] = lop_and_or(q2, 0x00C000C0u, 0x64006400u);
   } else if constexpr (!CB && BITS == 8) {
-    // (1024 + b) by byte permute into the fp16 mantissa, centre 128.
-    const uint4 xa = xv[w >> 1];
-    const uint32_t xlo = (w & 1) ? xa.z : xa.x;
-    const uint32_t xhi = (w & 1) ? xa.w : xa.y;
-    const uint32_t t0 = __byte_perm(q, 0x64646464u, 0x5140);
-    const uint32_t t1 = __byte_perm(q, 0x64646464u, 0x5342);
-    const half2 c0 = __hsub2(u2h2(t0), u2h2(0x64806480u));
-    const half2 c1 = __hsub2(u2h2(t1), u2h2(0x64806480u));
-    half2 a = __hmul2(c0, u2h2(xlo));
-    a = __hfma2(c1, u2h2(xhi), a);
-    return a;
+    P[0] = __byte_perm(q, 0x64646464u, 0x5140);                                         // 1024 + b
+    P[1] = __byte_perm(q, 0x64646464u, 0x5342);
   } else if constexpr (CB && BITS == 4) {
-    // lut: [256 bytes][32 lanes] half2 (v(lo)-C, v(hi)-C); `lut` is lane-offset.
-    const uint4 xa = xv[w];
-    const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w};
-    half2 a = __float2half2_rn(0.f);
+    // lut: [256 bytes][32 lanes] half2 (v(lo)-C, v(hi)-C)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t b = (q >> (8 * i)) & 0xFFu;
-      const uint32_t v = *reinterpret_cast<const uint32_t*>(lut + b * 128u);
-      a = __hfma2(u2h2(v), u2h2(xs[i]), a);
-    }
-    return a;
+    for (int i = 0; i < 4; ++i) P[i] = *reinterpret_cast<const uint32_t*>(lut + ((q >> (8 * i)) & 0xFFu) * 128u);
   } else if constexpr (CB && BITS == 2) {
-    // lut: [256][32 lanes] uint2 = two half2 (crumbs 0,1 | 2,3).
-    const uint4 xa = xv[2 * w];
-    const uint4 xb = xv[2 * w + 1];
-    const uint32_t xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    half2 a = __float2half2_rn(0.f);
+    // lut: [256][32 lanes] uint2 = two half2 (crumbs 0,1 | 2,3)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t b = (q >> (8 * i)) & 0xFFu;
-      const uint2 v = *reinterpret_cast<const uint2*>(lut + b * 256u);
-      a = __hfma2(u2h2(v.x), u2h2(xs[2 * i]), a);
-      a = __hfma2(u2h2(v.y), u2h2(xs[2 * i + 1]), a);
+      const uint2 v = *reinterpret_cast<const uint2*>(lut + ((q >> (8 * i)) & 0xFFu) * 256u);
+      P[2 * i] = v.x;
+      P[2 * i + 1] = v.y;
     }
-    return a;
   } else {
-    // CB && BITS == 8: lut [256][32 lanes] u32 holding one fp16 in the low half.
-    const uint4 xa = xv[w >> 1];
-    const uint32_t xlo = (w & 1) ? xa.z : xa.x;
-    const uint32_t xhi = (w & 1) ? xa.w : xa.y;
+    // CB && BITS == 8: lut [256][32 lanes] u32 holding one fp16 in the low half
     const uint32_t v0 = *reinterpret_cast<const uint32_t*>(lut + (q & 0xFFu) * 128u);
     const uint32_t v1 = *reinterpret_cast<const uint32_t*>(lut + ((q >> 8) & 0xFFu) * 128u);
     const uint32_t v2 = *reinterpret_cast<const uint32_t*>(lut + ((q >> 16) & 0xFFu) * 128u);
     const uint32_t v3 = *reinterpret_cast<const uint32_t*>(lut + (q >> 24) * 128u);
-    half2 a = __hmul2(u2h2(__byte_perm(v0, v1, 0x5410)), u2h2(xlo));
-    a = __hfma2(u2h2(__byte_perm(v2, v3, 0x5410)), u2h2(xhi), a);
-    return a;
+    P[0] = __byte_perm(v0, v1, 0x5410);
+    P[1] = __byte_perm(v2, v3, 0x5410);
   }
 }
 
-// Raw (not yet decoded) metadata of one (row, group), loaded ahead of use.
-struct MetaRaw {
-  uint32_t a, b, c;
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct Args {
+  QW q;
+  const void* x;
+  int x_dtype;
+  int64_t x_stride;
+  int64_t m0;          // first token of this pass
+  int mt;              // tokens in this pass (<= kMaxTok)
+  const void* bias;
+  int bias_dtype;
+  void* out;
+  int out_dtype;
+  int64_t out_stride;
+  float* partials;     // [grid][2][kTileRows][kMaxTok]
+  int* counters;       // [row blocks]
+  int* err;            // wait-timeout flag
+  uint32_t tiles;      // row_blocks * kgroups
+  uint32_t kgroups;    // tiles per row block
+  uint32_t grid;
+  int stages;          // ring depth
+  int stage_bytes;     // packed rows + metadata of one stage
+  int meta_row_words;  // 32-bit words per metadata row slot (per array)
+  int n_chunks;        // 16-byte chunks covering padded_cols
+  int seg_chunks;      // chunks per scale segment: min(4, group bytes / 16)
+  int gpt;             // groups per full tile row
+  int gbytes_shift;    // log2(bytes of packed codes per group)
+  int max_owned_rows;  // capacity of the per-CTA epilogue table
+  int x_vec16;         // activation rows are 16-byte aligned
+  int meta_bulk;       // metadata rows are 16-byte aligned: stream them with bulk copies
+  float center;        // C for uniform grids (codebooks use their midpoint)
 };
 
-template <bool DQ>
-__device__ __forceinline__ MetaRaw load_meta(const QW& q, uint32_t flat, int dq_shift) {
-  MetaRaw m;
-  if constexpr (DQ) {
-    const uint32_t sup = dq_shift >= 0 ? (flat >> dq_shift) : flat / (uint32_t)q.dq_gs;
-    m.a = (uint32_t)__ldg(q.dqs_codes + flat) | ((uint32_t)__ldg(q.dqg_codes + flat) << 8);
-    m.b = h22u(__ldg(q.dqs_meta + sup));
-    m.c = h22u(__ldg(q.dqg_meta + sup));
-  } else {
-    m.a = __half_as_ushort(__ldg(q.scale + flat));
-    m.b = __half_as_ushort(__ldg(q.gmin + flat));
-    m.c = 0;
-  }
-  return m;
+__device__ __forceinline__ uint32_t cta_of(uint64_t t, uint64_t U, uint64_t G) {
+  return (uint32_t)(((t + 1) * G + U - 1) / U - 1);
 }
 
-template <bool DQ>
-__device__ __forceinline__ float2 decode_meta(const MetaRaw& m) {
-  if constexpr (DQ) {
-    const float2 ms = __half22float2(u2h2(m.b));
-    const float2 mg = __half22float2(u2h2(m.c));
-    const float s = __fadd_rn(__fmul_rn((float)(m.a & 0xFFu), ms.x), ms.y);
-    const float g = __fadd_rn(__fmul_rn((float)(m.a >> 8), mg.x), mg.y);
-    return make_float2(s, g);
-  } else {
-    return make_float2(h2f((uint16_t)m.a), h2f((uint16_t)m.b));
-  }
-}
-
-struct Stage {
-  uint4 w[kR];
-  MetaRaw m[kR];
-};
-
-// Unit position (row group, 512-byte chunk), advanced incrementally so the
-// streaming loop does no integer division.
-struct Cursor {
-  uint32_t rg, ch;
-};
-
-template <int BITS, bool DQ>
-__device__ __forceinline__ void load_stage(Stage& st, const Args& a, const Cursor c, int lane) {
-  const uint32_t boff = c.ch * 512u + lane * 16u;
-  const bool valid = boff < (uint32_t)a.q.row_bytes;
-  const uint32_t g = boff >> a.gbytes_shift;
-#pragma unroll
-  for (int r = 0; r < kR; ++r) {
-    const uint32_t row = c.rg * kR + r;
-    if (valid && row < (uint32_t)a.q.rows) {
-      st.w[r] = ldg_stream_v4(a.q.packed + (size_t)row * (size_t)a.q.row_bytes + boff);
-      st.m[r] = load_meta<DQ>(a.q, row * (uint32_t)a.q.n_groups + g, a.dq_shift);
-    } else {
-      st.w[r] = make_uint4(0, 0, 0, 0);
-      st.m[r] = MetaRaw{0, 0, 0};
-    }
-  }
-}
-
-__device__ __forceinline__ void advance(Cursor& c, uint32_t chunks) {
-  if (++c.ch == chunks) {
-    c.ch = 0;
-    ++c.rg;
-  }
-}
-
-// Index of the warp whose unit range contains unit u (ranges are
-// [floor(U*w/W), floor(U*(w+1)/W))).
-__device__ __forceinline__ uint32_t warp_of(uint64_t u, uint64_t U, uint64_t W) {
-  return (uint32_t)(((u + 1) * W + U - 1) / U - 1);
-}
-
-template <int MT>
-__device__ void finish_rows(const Args& a, uint32_t rg, float (&tot)[kR][MT], int lane) {
-  // Outlier correction (CSR walk, lanes split the row's entries), bias, store.
-#pragma unroll
-  for (int r = 0; r < kR; ++r) {
-    const int64_t row = (int64_t)rg * kR + r;
-    if (row >= a.q.rows) break;
-    float c[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) c[m] = 0.f;
-    if (a.q.n_outliers > 0) {
-      const int o0 = __ldg(a.q.orow_ptr + row), o1 = __ldg(a.q.orow_ptr + row + 1);
-      for (int j = o0 + lane; j < o1; j += 32) {
-        const int64_t col = __ldg(a.q.ocol + j);
-        const float d = __half2float(__ldg(a.q.odelta + j));
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-          if (m < a.mt) c[m] += load_f(a.x, a.x_dtype, (a.m0 + m) * a.x_stride + col) * d;
-      }
-#pragma unroll
-      for (int m = 0; m < MT; ++m) c[m] = warp_sum(c[m]);
-    }
-    const float b = a.bias ? load_f(a.bias, a.bias_dtype, row) : 0.f;
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (lane == m && m < a.mt)
-        store_f(a.out, a.out_dtype, (a.m0 + m) * a.out_stride + row, tot[r][m] + c[m] + b);
-  }
-}
-
-template <int BITS, bool CB, bool DQ, int MT>
-__global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const Args a) {
+template <int BITS, bool CB, bool DQ, int SEG>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemv_kernel(const Args a) {
   using G = Geo<BITS>;
-  extern __shared__ __align__(16) char smem[];
+  extern __shared__ __align__(128) char smem[];
   constexpr int LUT_BYTES = !CB ? 0 : (BITS == 2 ? 256 * 32 * 8 : 256 * 32 * 4);
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const uint32_t gw = blockIdx.x * kWarps + warp;
-  const uint64_t U = a.units, W = a.total_warps;
-  const uint32_t u_begin = (uint32_t)(U * gw / W);
-  const uint32_t u_end = (uint32_t)(U * (gw + 1) / W);
+  constexpr int E = DQ ? 4 : 2;                      // metadata elements per 32-bit word
+  const int S = a.stages;
+  // layout: [stages: rows | meta][LUT][B fragments][segment (f, sum)][epilogue][reduction][barriers]
+  char* stages = smem;
+  char* lut = smem + S * a.stage_bytes;
+  const int n_mma = a.n_chunks * G::MPW;
+  const int tok_stride = n_mma * 4 + 4;              // uint2 per token (+32 B pad)
+  uint2* xb = reinterpret_cast<uint2*>(lut + LUT_BYTES);
+  const int n_seg = a.n_chunks / a.seg_chunks;
+  // per (token, segment): (2^e, sum x, sum of the uniform-grid offsets 1024/m * x~, 0)
+  float4* sx = reinterpret_cast<float4*>(xb + a.mt * tok_stride);
+  float* epi = reinterpret_cast<float*>(sx + a.mt * n_seg);
+  float* red = epi + a.max_owned_rows * kMaxTok;
+  int* o_ptr = reinterpret_cast<int*>(red + kConsumerWarps * kTileRows * kMaxTok);   // [owned rows + 1]
+  int* o_col = o_ptr + a.max_owned_rows + 4;                                            // [kOutCap]
+  float* o_dl = reinterpret_cast<float*>(o_col + kOutCap);                              // [kOutCap]
+  float* o_bias = o_dl + kOutCap;                                                       // [owned rows]
+  float* cbuf = o_bias + a.max_owned_rows + 4;                                           // [kCbuf]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cbuf + kCbuf);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxStages;
+  int* s_flag = reinterpret_cast<int*>(bars + 2 * kMaxStages);
+  // per-stage metadata region (after the packed rows): plain: scale rows,
+  // gmin rows; DQ: scale codes, gmin codes, scale supers, gmin supers
+  const int mrw = a.meta_row_words;
 
-  char* lut = smem;
-  __half* xs = reinterpret_cast<__half*>(smem + LUT_BYTES);
-  const int64_t x_tok = (int64_t)a.n_chunks_x * G::CHUNK_W;  // halves per token
-  float2* sx = reinterpret_cast<float2*>(xs + MT * x_tok);
-  const int n_spans = a.n_chunks_x * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t U = a.tiles, GR = a.grid;
+  const uint32_t t0 = (uint32_t)(U * blockIdx.x / GR), t1 = (uint32_t)(U * (blockIdx.x + 1) / GR);
+  const uint32_t KG = a.kgroups;
+  const uint32_t NGR = (uint32_t)a.q.n_groups;
 
-  // 1. Start streaming this warp's first weights (independent of x).
-  constexpr int D = 3;
-  Stage st[D];
-  const uint32_t first_rg = u_begin / a.chunks;
-  Cursor pf{first_rg, u_begin - first_rg * a.chunks};  // prefetch cursor
-#pragma unroll
-  for (int d = 0; d < D; ++d)
-    if (u_begin + d < u_end) {
-      load_stage<BITS, DQ>(st[d], a, pf, lane);
-      advance(pf, a.chunks);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full + i, a.meta_bulk ? 1 : 1 + 32);   // expect_tx arrival (+ 32 async-copy arrivals)
+      mbar_init(empty + i, kConsumerWarps);
     }
+    fence_barrier_init();
+  }
+  __syncthreads();
 
-  // 2. Codebook lookup table (per-lane copies: conflict-free random access).
-  //    Centre C = midpoint of the codebook range keeps the fp16 levels small.
+  // ------------------------------------------------------------------ producer
+  if (warp == kConsumerWarps) {
+    pdl_launch_dependents();
+    uint32_t rb = t0 / KG, kg = t0 - rb * KG;
+    for (uint32_t i = 0; t0 + i < t1; ++i) {
+      const int s = i % S;
+      if (i >= (uint32_t)S && !mbar_wait(empty + s, ((i / S) - 1) & 1, a.err, 1)) break;
+      char* st = stages + s * a.stage_bytes;
+      uint32_t* meta = reinterpret_cast<uint32_t*>(st + kTileRows * kPitch);
+      const uint32_t row0 = rb * kTileRows;
+      const uint32_t nrows = (uint32_t)(a.q.rows - (int64_t)row0 < kTileRows ? a.q.rows - (int64_t)row0 : kTileRows);
+      const uint32_t rbytes = (uint32_t)(a.q.row_bytes - (int64_t)kg * kTileK < kTileK ? a.q.row_bytes - (int64_t)kg * kTileK : kTileK);
+      const uint32_t g0 = kg * (uint32_t)a.gpt;
+      if (a.meta_bulk) {
+        // aligned metadata: one bulk copy per (array, row) + one per super array
+        const uint32_t ng = min((uint32_t)a.gpt, NGR - g0);            // groups in this tile
+        const uint32_t mb = ng * (DQ ? 1u : 2u);                         // bytes per metadata row
+        uint32_t sup_al = 0, sup_bytes = 0;
+        if constexpr (DQ) {
+          const uint32_t s_lo = (row0 * NGR + g0) / (uint32_t)a.q.dq_gs;
+          const uint32_t s_hi = ((row0 + nrows - 1) * NGR + g0 + ng - 1) / (uint32_t)a.q.dq_gs;
+          sup_al = s_lo & ~3u;
+          sup_bytes = ((s_hi - sup_al + 4) & ~3u) * 4u;
+          const uint32_t n_sup_all = (uint32_t)((a.q.rows * (int64_t)NGR + a.q.dq_gs - 1) / a.q.dq_gs);
+          sup_bytes = min(sup_bytes, (n_sup_all - sup_al) * 4u);
+        }
+        if (lane == 0) mbar_arrive_expect_tx(full + s, nrows * rbytes + 2 * nrows * mb + 2 * sup_bytes);
+        __syncwarp();
+        if (lane < (int)nrows)
+          bulk_load(st + lane * kPitch,
+                    a.q.packed + (size_t)(row0 + lane) * (size_t)a.q.row_bytes + (size_t)kg * kTileK, rbytes, full + s);
+        {
+          const int arr = lane >> 4, r = lane & 15;
+          if (r < (int)nrows) {
+            const uint32_t e = (row0 + r) * NGR + g0;
+            const void* src;
+            if constexpr (DQ)
+              src = (arr == 0 ? a.q.dqs_codes : a.q.dqg_codes) + e;
+            else
+              src = (arr == 0 ? a.q.scale : a.q.gmin) + e;
+            bulk_load(meta + (arr * kTileRows + r) * mrw, src, mb, full + s);
+          }
+        }
+        if constexpr (DQ) {
+          if (lane < 2)
+            bulk_load(meta + 2 * kTileRows * mrw + lane * kMaxSupers,
+                      (lane == 0 ? a.q.dqs_meta : a.q.dqg_meta) + sup_al, sup_bytes, full + s);
+        }
+      } else {
+        if (lane == 0) mbar_arrive_expect_tx(full + s, nrows * rbytes);
+        __syncwarp();
+        if (lane < (int)nrows)
+          bulk_load(st + lane * kPitch,
+                    a.q.packed + (size_t)(row0 + lane) * (size_t)a.q.row_bytes + (size_t)kg * kTileK, rbytes, full + s);
+        // unaligned metadata: 4-byte async copies of the aligned-down words
+        for (int ar = 0; ar < 2 * kTileRows; ++ar) {
+          const int arr = ar / kTileRows, r = ar - arr * kTileRows;
+          const uint32_t row = row0 + r;
+          const bool v = row < (uint32_t)a.q.rows;
+          const uint32_t e0 = v ? ((row * NGR + g0) & ~(uint32_t)(E - 1)) : 0u;
+          for (int wd = lane; wd < mrw; wd += 32) {
+            const uint32_t e = e0 + wd * E;
+            const bool in = v && e < (uint32_t)(a.q.rows * NGR);
+            const void* src;
+            if constexpr (DQ)
+              src = (arr == 0 ? a.q.dqs_codes : a.q.dqg_codes) + (in ? e : 0u);
+            else
+              src = (arr == 0 ? a.q.scale : a.q.gmin) + (in ? e : 0u);
+            cp_async4(meta + ar * mrw + wd, src, in ? 4 : 0);
+          }
+        }
+        if constexpr (DQ) {
+          uint32_t* sup = meta + 2 * kTileRows * mrw;
+          const uint32_t s_al = ((row0 * NGR + g0) / (uint32_t)a.q.dq_gs) & ~3u;
+          const uint32_t n_sup_all = (uint32_t)((a.q.rows * (int64_t)NGR + a.q.dq_gs - 1) / a.q.dq_gs);
+          for (int j = lane; j < kMaxSupers; j += 32) {
+            const uint32_t sidx = s_al + j;
+            const bool in = sidx < n_sup_all;
+            cp_async4(sup + j, a.q.dqs_meta + (in ? sidx : 0u), in ? 4 : 0);
+            cp_async4(sup + kMaxSupers + j, a.q.dqg_meta + (in ? sidx : 0u), in ? 4 : 0);
+          }
+        }
+        cp_async_arrive(full + s);
+      }
+      if (++kg == KG) {
+        kg = 0;
+        ++rb;
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
   float center = a.center;
   if constexpr (CB) {
     const float* cb = a.q.codebook;
     center = 0.5f * (__ldg(cb) + __ldg(cb + (1 << BITS) - 1));
-    for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
+    for (int i = threadIdx.x; i < 256 * 32; i += kConsumerThreads) {
       const int b = i >> 5, l = i & 31;
       if constexpr (BITS == 4) {
         const half2 v = __floats2half2_rn(__ldg(cb + (b & 15)) - center, __ldg(cb + (b >> 4)) - center);
@@ -340,190 +348,317 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const Args a) {
     }
   }
 
-  // 3. Wait for the producer of x (programmatic dependent launch), stage it:
-  //    one thread per 8 consecutive activations; the SPAN/8 threads of a span
-  //    (an aligned lane group) reduce its max |x| and sum with shuffles.
+  // row blocks whose first tile this CTA owns (it adds their bias and outliers)
+  const uint32_t rb_own0 = (t0 + KG - 1) / KG, rb_own1 = (t1 + KG - 1) / KG;
+  const int n_own = (int)(rb_own1 - rb_own0) * kTileRows;
+
+  // outlier slice (CSR bounds, columns, deltas) and bias of the owned rows:
+  // constant buffers, loaded before waiting on the producer of x
+  const int64_t own_row0 = (int64_t)rb_own0 * kTileRows;
+  const int64_t rows_left = a.q.rows - own_row0;
+  const int n_own_rows = rows_left <= 0 ? 0 : (rows_left < n_own ? (int)rows_left : n_own);
+  for (int i = threadIdx.x; i <= n_own_rows; i += kConsumerThreads)
+    o_ptr[i] = a.q.n_outliers > 0 ? __ldg(a.q.orow_ptr + own_row0 + i) : 0;
+  for (int i = threadIdx.x; i < n_own_rows; i += kConsumerThreads)
+    o_bias[i] = a.bias ? load_f(a.bias, a.bias_dtype, own_row0 + i) : 0.f;
+  named_bar_sync(1, kConsumerThreads);
+  const int o_base = n_own_rows > 0 ? o_ptr[0] : 0;
+  const int o_cnt = n_own_rows > 0 ? o_ptr[n_own_rows] - o_base : 0;
+  for (int j = threadIdx.x; j < min(o_cnt, kOutCap); j += kConsumerThreads) {
+    o_col[j] = __ldg(a.q.ocol + o_base + j);
+    o_dl[j] = __half2float(__ldg(a.q.odelta + o_base + j));
+  }
+
+  // x is produced by the previous kernel in the stream (programmatic launch)
   pdl_wait_primary();
   {
-    constexpr int TPS = G::SPAN / 8;
-    const uint32_t per_tok = (uint32_t)(a.q.padded_cols / 8);
-    const uint32_t items = MT * per_tok;
-    for (uint32_t base = 0; base < items; base += kThreads) {
+    // one thread per 16 consecutive activations of one token: load, reduce the
+    // segment's max |x| and sum across its threads, write the B fragments
+    const int seg_k = a.seg_chunks * G::KPC;
+    const int tps = seg_k / 16;                      // threads per segment (power of two)
+    const uint32_t per_tok = (uint32_t)(a.q.padded_cols / 16);
+    const uint32_t items = a.mt * per_tok;
+    for (uint32_t base = 0; base < items; base += kConsumerThreads) {
       const uint32_t it = base + threadIdx.x;
       const bool live = it < items;
-      const uint32_t m = live ? it / per_tok : 0;
-      const uint32_t k0 = live ? (it - m * per_tok) * 8 : 0;
-      const bool tok = live && (int)m < a.mt;
-      const int64_t xoff = (a.m0 + m) * a.x_stride + k0;
-      float v[8];
-      if (tok && a.x_vec16 && k0 + 8 <= (uint32_t)a.q.cols) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + xoff));
-        const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
+      const uint32_t n = live ? it / per_tok : 0;
+      const uint32_t k0 = live ? (it - n * per_tok) * 16 : 0;
+      const int64_t xo = (a.m0 + n) * a.x_stride + k0;
+      float v[16];
+      if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
+        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + xo);
+        const uint4 r0 = __ldg(p), r1 = __ldg(p + 1);
+        const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 8; ++j) {
           if (a.x_dtype == TS_F16) {
-            const float2 f = __half22float2(u2h2(r4[j]));
+            const float2 f = __half22float2(u2h2(rw[j]));
             v[2 * j] = f.x;
             v[2 * j + 1] = f.y;
           } else {
-            v[2 * j] = __uint_as_float(r4[j] << 16);
-            v[2 * j + 1] = __uint_as_float(r4[j] & 0xFFFF0000u);
+            v[2 * j] = __uint_as_float(rw[j] << 16);
+            v[2 * j + 1] = __uint_as_float(rw[j] & 0xFFFF0000u);
           }
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          v[j] = (tok && k0 + j < (uint32_t)a.q.cols) ? load_f(a.x, a.x_dtype, xoff + j) : 0.f;
+        for (int j = 0; j < 16; ++j)
+          v[j] = (live && k0 + j < (uint32_t)a.q.cols) ? load_f(a.x, a.x_dtype, xo + j) : 0.f;
       }
       float mx = 0.f, sum = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 16; ++j) {
         mx = fmaxf(mx, fabsf(v[j]));
         sum += v[j];
       }
-#pragma unroll
-      for (int o = TPS / 2; o > 0; o >>= 1) {
+      for (int o = tps / 2; o > 0; o >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         sum += __shfl_xor_sync(0xffffffffu, sum, o);
       }
-      int e = 0;
-      if (mx > 0.f) frexpf(mx, &e);
-      if (live) {
-        const uint32_t sp = k0 / G::SPAN;          // span index within the token
-        const int j0 = (int)(k0 - sp * G::SPAN);   // this thread's offset in the span
-        if (j0 == 0) sx[m * n_spans + sp] = make_float2(ldexpf(1.f, e), sum);
-        __half* dst = xs + m * x_tok + (int64_t)(sp >> 5) * G::CHUNK_W;
-        const int l = (int)(sp & 31);
+      // power-of-two scale 2^e with max|x| / 2^e in [0.5, 1): exponent bits
+      const int e = mx > 0.f ? min(126, (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 126) : 0;
+      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+      float hx[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int jj = j0 + j;
-          const int word = jj / G::WORD_W, jw = jj - word * G::WORD_W;
-          const int o = word * G::WORD_W + word_pos<BITS, CB>(jw);
-          dst[((o >> 3) * 32 + l) * 8 + (o & 7)] = __float2half_rn(ldexpf(v[j], -e));
+      for (int j = 0; j < 16; ++j) hx[j] = v[j] * inv;
+      // B fragments (x~ / m of each pair) and, for uniform grids, the constant
+      // sum over k of (1024 / m_k) * x~_k carried by the raw unpacked codes
+      float xc = 0.f;
+      uint2 frag[16 / G::KPW][G::MPW];
+#pragma unroll
+      for (int wb = 0; wb < 16 / G::KPW; ++wb) {
+#pragma unroll
+        for (int m = 0; m < G::MPW; ++m) {
+          uint32_t bw[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int pr = 2 * m + h;
+            const int2 o = pair_off<BITS, CB>(pr);
+            const float im = 1.f / pair_mult<BITS, CB>(pr);
+            const half2 hv = __floats2half2_rn(hx[wb * G::KPW + o.x] * im, hx[wb * G::KPW + o.y] * im);
+            bw[h] = h22u(hv);
+            if constexpr (!CB) {
+              const float2 f2 = __half22float2(hv);
+              xc += 1024.f * (f2.x + f2.y);
+            }
+          }
+          frag[wb][m] = make_uint2(bw[0], bw[1]);
+        }
+      }
+      for (int o = tps / 2; o > 0; o >>= 1) xc += __shfl_xor_sync(0xffffffffu, xc, o);
+      if (live) {
+        const uint32_t sg = k0 / seg_k;
+        if (k0 % seg_k == 0)
+          sx[n * n_seg + sg] = make_float4(__uint_as_float((uint32_t)(e + 127) << 23), sum, xc, 0.f);
+#pragma unroll
+        for (int wb = 0; wb < 16 / G::KPW; ++wb) {
+          const uint32_t gwb = k0 / G::KPW + wb;     // global word-block index
+          const uint32_t ch = gwb >> 2, l = gwb & 3;
+#pragma unroll
+          for (int m = 0; m < G::MPW; ++m) xb[n * tok_stride + (ch * G::MPW + m) * 4 + l] = frag[wb][m];
         }
       }
     }
   }
-  __syncthreads();
-  pdl_launch_dependents();
+  named_bar_sync(1, kConsumerThreads);
+  {
+    // epilogue table: bias + sum over the row's outliers of x[:, col] * delta.
+    // Contributions are computed one thread per (outlier, token) into `cbuf`
+    // (activations read back from the staged fragments: x = x~ * m * 2^e),
+    // then summed per row in outlier order (deterministic), in passes of
+    // kCbuf / mt outliers.
+    const int seg_k = a.seg_chunks * G::KPC;
+    const int seg_sh = 31 - __clz(seg_k);
+    for (int i = threadIdx.x; i < n_own; i += kConsumerThreads)
+#pragma unroll
+      for (int n = 0; n < kMaxTok; ++n) epi[i * kMaxTok + n] = i < n_own_rows ? o_bias[i] : 0.f;
+    const int per_pass = kCbuf / a.mt;
+    for (int j0 = 0; j0 < o_cnt; j0 += per_pass) {
+      const int jn = min(per_pass, o_cnt - j0);
+      named_bar_sync(1, kConsumerThreads);
+      for (int it = threadIdx.x; it < jn * a.mt; it += kConsumerThreads) {
+        const int jj = it / a.mt, n = it - jj * a.mt, j = j0 + jj;
+        const int col = j < kOutCap ? o_col[j] : __ldg(a.q.ocol + o_base + j);
+        const float d = j < kOutCap ? o_dl[j] : __half2float(__ldg(a.q.odelta + o_base + j));
+        const int wb = col / G::KPW, o = col - wb * G::KPW;
+        int p, hi;
+        if (!CB && BITS == 4) { p = o & 3; hi = o >> 2; }
+        else if (!CB && BITS == 2) { p = o & 7; hi = o >> 3; }
+        else { p = o >> 1; hi = o & 1; }
+        const int J = (wb >> 2) * G::MPW + (p >> 1), l = wb & 3;
+        const uint2 u = xb[n * tok_stride + J * 4 + l];
+        const uint32_t hw = (p & 1) ? u.y : u.x;
+        const float xv = __half2float(__ushort_as_half((uint16_t)(hw >> (16 * hi)))) * pair_mult<BITS, CB>(p) *
+                         sx[n * n_seg + (col >> seg_sh)].x;
+        cbuf[jj * a.mt + n] = xv * d;
+      }
+      named_bar_sync(1, kConsumerThreads);
+      for (int it = threadIdx.x; it < n_own_rows * a.mt; it += kConsumerThreads) {
+        const int i = it / a.mt, n = it - i * a.mt;
+        const int lo = max(o_ptr[i] - o_base, j0), hi = min(o_ptr[i + 1] - o_base, j0 + jn);
+        float c = epi[i * kMaxTok + n];
+        for (int j = lo; j < hi; ++j) c += cbuf[(j - j0) * a.mt + n];
+        epi[i * kMaxTok + n] = c;
+      }
+    }
+  }
+  named_bar_sync(1, kConsumerThreads);
+  if (t0 >= t1) return;
 
-  if (u_begin >= u_end) return;
+  const int q = lane >> 2, l = lane & 3;   // rows q, q+8; token columns 2l, 2l+1
   const char* lut_lane = lut + lane * (BITS == 2 ? 8 : 4);
+  uint32_t rb = t0 / KG, kg = t0 - rb * KG;
+  const uint32_t first_rb = rb;
+  bool started_here = kg == 0;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};     // (q,2l) (q,2l+1) (q+8,2l) (q+8,2l+1)
+  const bool has_b = q < a.mt;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
 
-  float acc[kR][MT];
-#pragma unroll
-  for (int r = 0; r < kR; ++r)
-#pragma unroll
-    for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+  // per-lane constants of the tile loop
+  const uint2* xb_lane = xb + q * tok_stride + l;          // B fragment column of this lane's token
+  const float4* sx0 = sx + (2 * l) * n_seg;                 // segment stats of tokens 2l, 2l+1
+  const float4* sx1 = sx + (2 * l + 1) * n_seg;
+  const bool tok0 = 2 * l < a.mt, tok1 = 2 * l + 1 < a.mt;
+  const uint32_t slice_g = (uint32_t)(warp * kSlice) >> a.gbytes_shift;   // first group of the slice in the tile
 
-  uint32_t rg = first_rg;
-  uint32_t ch = u_begin - rg * a.chunks;
-  bool started_here = ch == 0;
-
-  for (uint32_t base = u_begin; base < u_end; base += D) {
+  for (uint32_t i = 0; t0 + i < t1; ++i) {
+    const int s = i % S;
+    const bool ok = mbar_wait(full + s, (i / S) & 1, a.err, 2);
+    const char* st = stages + s * a.stage_bytes;
+    const uint32_t* meta = reinterpret_cast<const uint32_t*>(st + kTileRows * kPitch);
+    const uint32_t g0 = kg * (uint32_t)a.gpt;
+    const uint32_t row_q = rb * kTileRows + q;
+    // metadata slot offsets of rows q, q+8 (element index of the tile's first group)
+    const uint32_t moff0 = ((row_q * NGR + g0) & (uint32_t)(E - 1)) + slice_g;
+    const uint32_t moff1 = (((row_q + 8) * NGR + g0) & (uint32_t)(E - 1)) + slice_g;
+    const uint32_t* mrow0 = meta + q * mrw;
+    const uint32_t* mrow1 = meta + (q + 8) * mrw;
+    uint32_t sup_lo = 0;
+    if constexpr (DQ) sup_lo = ((rb * kTileRows * NGR + g0) / (uint32_t)a.q.dq_gs) & ~3u;
+    const char* arow0 = st + q * kPitch + warp * kSlice + 4 * l;
+    const char* arow1 = arow0 + 8 * kPitch;
+    const uint32_t slice_byte0 = kg * (uint32_t)kTileK + warp * kSlice;
+    const int J_slice = (int)(slice_byte0 >> 4) * G::MPW;
+    const int gseg0 = (int)(slice_byte0 >> 4) / SEG;
+    constexpr int NSG = kSlice / 16 / SEG;  // scale segments per warp slice
 #pragma unroll
-    for (int d = 0; d < D; ++d) {
-      const uint32_t u = base + d;
-      if (u < u_end) {
-        const Stage cur = st[d];
-        if (u + D < u_end) {
-          load_stage<BITS, DQ>(st[d], a, pf, lane);
-          advance(pf, a.chunks);
-        }
-        const uint32_t boff = ch * 512u + lane * 16u;
-        if (boff < (uint32_t)a.q.row_bytes) {
-          const uint32_t sp = ch * 32 + lane;
-          float2 fx[MT];
+    for (int sg = 0; sg < NSG; ++sg) {
+      if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) break;
+      // two independent accumulator chains per segment
+      float cc[2][4];
 #pragma unroll
-          for (int m = 0; m < MT; ++m) fx[m] = sx[m * n_spans + sp];
+      for (int u = 0; u < 2; ++u) cc[u][0] = cc[u][1] = cc[u][2] = cc[u][3] = 0.f;
 #pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            if (m < a.mt) {
-              const uint4* xv = reinterpret_cast<const uint4*>(xs + m * x_tok + (int64_t)ch * G::CHUNK_W) + lane;
-              uint4 xl[G::VEC];  // vector v of this lane sits v*32 uint4s further
+      for (int cj = 0; cj < SEG; ++cj) {
+        const int cb = (sg * SEG + cj) * 16;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(arow0 + cb);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(arow1 + cb);
+        uint32_t P0[G::PPW], P1[G::PPW];
+        expand<BITS, CB>(w0, lut_lane, P0);
+        expand<BITS, CB>(w1, lut_lane, P1);
+        const int J0 = J_slice + (sg * SEG + cj) * G::MPW;
 #pragma unroll
-              for (int v = 0; v < G::VEC; ++v) xl[v] = xv[v * 32];
-#pragma unroll
-              for (int r = 0; r < kR; ++r) {
-                const uint32_t wq[4] = {cur.w[r].x, cur.w[r].y, cur.w[r].z, cur.w[r].w};
-                float p0 = 0.f, p1 = 0.f;
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                  const float2 f2 = __half22float2(word_dot<BITS, CB>(wq[w], xl, w, lut_lane));
-                  p0 += f2.x;
-                  p1 += f2.y;
-                }
-                const float2 sg = decode_meta<DQ>(cur.m[r]);
-                const float gprime = fmaf(center, sg.x, sg.y);
-                acc[r][m] = fmaf(sg.x * fx[m].x, p0 + p1, fmaf(gprime, fx[m].y, acc[r][m]));
-              }
-            }
-          }
-        }
-        const bool last_chunk = ch == a.chunks - 1;
-        if (last_chunk || u == u_end - 1) {
-          // ---- flush this row group ----
-          float tot[kR][MT];
-#pragma unroll
-          for (int r = 0; r < kR; ++r)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              tot[r][m] = warp_sum(acc[r][m]);
-              acc[r][m] = 0.f;
-            }
-          if (started_here && last_chunk) {
-            finish_rows<MT>(a, rg, tot, lane);
-          } else {
-            const int slot = (rg == first_rg) ? 0 : 1;
-            float* mine = a.partials + ((size_t)gw * 2 + slot) * (kR * MT);
-#pragma unroll
-            for (int r = 0; r < kR; ++r)
-#pragma unroll
-              for (int m = 0; m < MT; ++m)
-                if (lane == r * MT + m) mine[r * MT + m] = tot[r][m];
-            __threadfence();
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) old = atomicAdd(a.counters + rg, 1);
-            old = __shfl_sync(0xffffffffu, old, 0);
-            // pieces = distinct non-empty warps owning this row group's units
-            const uint64_t u0 = (uint64_t)rg * a.chunks;
-            int pieces = 1;
-            for (uint32_t c = 1, prev = warp_of(u0, U, W); c < a.chunks; ++c) {
-              const uint32_t w = warp_of(u0 + c, U, W);
-              pieces += w != prev;
-              prev = w;
-            }
-            if (old == pieces - 1) {
-              __threadfence();
-#pragma unroll
-              for (int r = 0; r < kR; ++r)
-#pragma unroll
-                for (int m = 0; m < MT; ++m) tot[r][m] = 0.f;
-              for (uint32_t c = 0, prev = 0xFFFFFFFFu; c < a.chunks; ++c) {
-                const uint32_t pw = warp_of(u0 + c, U, W);
-                if (pw == prev) continue;
-                prev = pw;
-                const uint32_t pfirst = (uint32_t)((U * pw / W) / a.chunks);
-                const float* src = a.partials + ((size_t)pw * 2 + (rg == pfirst ? 0 : 1)) * (kR * MT);
-#pragma unroll
-                for (int r = 0; r < kR; ++r)
-#pragma unroll
-                  for (int m = 0; m < MT; ++m) tot[r][m] += __ldcg(src + r * MT + m);
-              }
-              finish_rows<MT>(a, rg, tot, lane);
-              if (lane == 0) a.counters[rg] = 0;
-            }
-          }
-        }
-        if (last_chunk) {
-          ++rg;
-          ch = 0;
-          started_here = true;
-        } else {
-          ++ch;
+        for (int m = 0; m < G::MPW; ++m) {
+          uint2 bf = make_uint2(0u, 0u);
+          if (has_b) bf = xb_lane[(J0 + m) * 4];
+          mma16816(cc[(cj * G::MPW + m) & 1], P0[2 * m], P1[2 * m], P0[2 * m + 1], P1[2 * m + 1], bf.x, bf.y);
         }
       }
+      float c[4];
+#pragma unroll
+      for (int z = 0; z < 4; ++z) c[z] = cc[0][z] + cc[1][z];
+      // close: acc += (s f) (C - Xc) + (g + C_cb s) X for rows q, q+8
+      const float4 fx0 = tok0 ? sx0[gseg0 + sg] : zero4;
+      const float4 fx1 = tok1 ? sx1[gseg0 + sg] : zero4;
+      const uint32_t gi = (uint32_t)(sg * SEG * 16) >> a.gbytes_shift;   // group within the slice
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t* mr = r ? mrow1 : mrow0;
+        const uint32_t off = (r ? moff1 : moff0) + gi;
+        float sc, gm;
+        if constexpr (DQ) {
+          const uint32_t* sup = meta + 2 * kTileRows * mrw;
+          const uint32_t row = row_q + 8 * r;
+          const uint32_t sj = (row * NGR + g0 + slice_g + gi) / (uint32_t)a.q.dq_gs - sup_lo;
+          const float2 ms = __half22float2(u2h2(sup[sj]));
+          const float2 mg = __half22float2(u2h2(sup[kMaxSupers + sj]));
+          const float csv = (float)((mr[off >> 2] >> ((off & 3) * 8)) & 0xFFu);
+          const float cgv = (float)((mr[kTileRows * mrw + (off >> 2)] >> ((off & 3) * 8)) & 0xFFu);
+          sc = __fadd_rn(__fmul_rn(csv, ms.x), ms.y);
+          gm = __fadd_rn(__fmul_rn(cgv, mg.x), mg.y);
+        } else {
+          sc = h2f((uint16_t)(mr[off >> 1] >> ((off & 1) * 16)));
+          gm = h2f((uint16_t)(mr[kTileRows * mrw + (off >> 1)] >> ((off & 1) * 16)));
+        }
+        const float gp = fmaf(center, sc, gm);
+        acc[2 * r] = fmaf(sc * fx0.x, c[2 * r] - fx0.z, fmaf(gp, fx0.y, acc[2 * r]));
+        acc[2 * r + 1] = fmaf(sc * fx1.x, c[2 * r + 1] - fx1.z, fmaf(gp, fx1.y, acc[2 * r + 1]));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
+
+    const bool last_kg = kg == KG - 1;
+    if (last_kg || t0 + i + 1 == t1) {
+      // ---- flush row block rb: reduce the 8 warps' k-slices through smem ----
+      float* rw = red + warp * kTileRows * kMaxTok;
+      rw[q * kMaxTok + 2 * l] = acc[0];
+      rw[q * kMaxTok + 2 * l + 1] = acc[1];
+      rw[(q + 8) * kMaxTok + 2 * l] = acc[2];
+      rw[(q + 8) * kMaxTok + 2 * l + 1] = acc[3];
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      named_bar_sync(1, kConsumerThreads);
+      const int t = threadIdx.x;                 // t < 128: (row t/8, token t%8)
+      const int rr = t >> 3, n = t & 7;
+      const int64_t row = (int64_t)rb * kTileRows + rr;
+      float tot = 0.f;
+      if (t < kTileRows * kMaxTok) {
+        for (int w = 0; w < kConsumerWarps; ++w) tot += red[(w * kTileRows + rr) * kMaxTok + n];
+        if (started_here) tot += epi[((rb - rb_own0) * kTileRows + rr) * kMaxTok + n];
+      }
+      if (started_here && last_kg) {
+        if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
+          store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row, tot);
+      } else {
+        const int slot = rb == first_rb ? 0 : 1;
+        if (t < kTileRows * kMaxTok)
+          a.partials[((size_t)blockIdx.x * 2 + slot) * (kTileRows * kMaxTok) + t] = tot;
+        __threadfence();
+        named_bar_sync(1, kConsumerThreads);
+        if (t == 0) *s_flag = atomicAdd(a.counters + rb, 1);
+        named_bar_sync(1, kConsumerThreads);
+        const int old = *s_flag;
+        const uint64_t u0 = (uint64_t)rb * KG;
+        int pieces = 1;
+        for (uint32_t cc = 1, prev = cta_of(u0, U, GR); cc < KG; ++cc) {
+          const uint32_t w = cta_of(u0 + cc, U, GR);
+          pieces += w != prev;
+          prev = w;
+        }
+        if (old == pieces - 1) {
+          __threadfence();
+          float sum = 0.f;
+          for (uint32_t cc = 0, prev = 0xFFFFFFFFu; cc < KG; ++cc) {
+            const uint32_t pc = cta_of(u0 + cc, U, GR);
+            if (pc == prev) continue;
+            prev = pc;
+            const uint32_t pfirst = (uint32_t)((U * pc / GR) / KG);
+            if (t < kTileRows * kMaxTok)
+              sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) + t);
+          }
+          if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
+            store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row, sum);
+          if (t == 0) a.counters[rb] = 0;
+        }
+      }
+      named_bar_sync(1, kConsumerThreads);  // `red` and `s_flag` are reused by the next flush
+    }
+    if (last_kg) {
+      kg = 0;
+      ++rb;
+      started_here = true;
+    } else {
+      ++kg;
     }
   }
 }
@@ -535,9 +670,62 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const Args a) {
 // ---------------------------------------------------------------------------
 namespace {
 
-template <int BITS, bool CB, bool DQ, int MT>
-int launch_one(const gemv::Args& a, int blocks_per_sm_cap, cudaStream_t stream, size_t smem) {
-  auto kern = gemv::qgemv_kernel<BITS, CB, DQ, MT>;
+int ilog2(int64_t v) {
+  int r = 0;
+  while ((int64_t(1) << (r + 1)) <= v) ++r;
+  return r;
+}
+
+struct Plan {
+  uint32_t tiles, kgroups, grid;
+  int n_chunks, seg_chunks, gpt, meta_row_words, stage_bytes, max_owned_rows;
+};
+
+int lut_bytes(const ts_qweight& w) { return w.codebook ? (w.bits == 2 ? 256 * 32 * 8 : 256 * 32 * 4) : 0; }
+
+Plan make_plan(const ts_qweight& w) {
+  Plan p;
+  const int64_t gbytes = (int64_t)w.group_size * w.bits / 8;
+  const int E = w.dq_scale_codes ? 4 : 2;
+  p.kgroups = (uint32_t)((w.packed_row_bytes + gemv::kTileK - 1) / gemv::kTileK);
+  const uint32_t rbs = (uint32_t)((w.rows + gemv::kTileRows - 1) / gemv::kTileRows);
+  p.tiles = rbs * p.kgroups;
+  p.grid = std::max<uint32_t>(1, std::min<uint32_t>((uint32_t)sm_count(), p.tiles));
+  p.n_chunks = (int)(w.padded_cols * w.bits / 128);
+  p.seg_chunks = (int)std::min<int64_t>(4, gbytes / 16);
+  p.gpt = (int)(gemv::kTileK / gbytes);
+  p.meta_row_words = (int)align_up((size_t)((p.gpt + 2 * (E - 1)) / E), 4);  // 16-byte slots
+  size_t meta = (size_t)2 * gemv::kTileRows * p.meta_row_words * 4;
+  if (w.dq_scale_codes) meta += (size_t)2 * gemv::kMaxSupers * 4;
+  p.stage_bytes = (int)align_up((size_t)gemv::kTileRows * gemv::kPitch + meta, 128);
+  const uint32_t per_cta = (p.tiles + p.grid - 1) / p.grid;
+  p.max_owned_rows = (int)((per_cta / p.kgroups + 2) * gemv::kTileRows);
+  return p;
+}
+
+// shared memory besides the stage ring, for `mt` tokens
+size_t fixed_smem(const ts_qweight& w, const Plan& p, int mt) {
+  const int mpw = 8 / w.bits;
+  const size_t n_mma = (size_t)p.n_chunks * mpw;
+  const size_t n_seg = (size_t)p.n_chunks / p.seg_chunks;
+  return lut_bytes(w) + (size_t)mt * (n_mma * 4 + 4) * 8 + (size_t)mt * n_seg * 16 +
+         (size_t)p.max_owned_rows * gemv::kMaxTok * 4 +
+         (size_t)gemv::kConsumerWarps * gemv::kTileRows * gemv::kMaxTok * 4 +
+         (size_t)(p.max_owned_rows + 4) * 4 + (size_t)gemv::kOutCap * 8 + (size_t)(p.max_owned_rows + 4) * 4 +
+         (size_t)gemv::kCbuf * 4 + 2 * gemv::kMaxStages * 8 + 64;
+}
+
+size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024); }
+
+int stages_for(const ts_qweight& w, const Plan& p, int mt) {
+  const size_t f = fixed_smem(w, p, mt);
+  if (f >= smem_cap()) return 0;
+  return (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - f) / p.stage_bytes);
+}
+
+template <int BITS, bool CB, bool DQ, int SEG>
+int launch_one(const gemv::Args& a, cudaStream_t stream, size_t smem) {
+  auto kern = gemv::qgemv_kernel<BITS, CB, DQ, SEG>;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -547,10 +735,8 @@ int launch_one(const gemv::Args& a, int blocks_per_sm_cap, cudaStream_t stream, 
     configured_dev = dev;
     configured_smem = smem;
   }
-  const int grid = (int)(a.total_warps / gemv::kWarps);
-  (void)blocks_per_sm_cap;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(a.grid);
   cfg.blockDim = dim3(gemv::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -565,61 +751,49 @@ int launch_one(const gemv::Args& a, int blocks_per_sm_cap, cudaStream_t stream, 
 }
 
 template <int BITS, bool CB, bool DQ>
-int launch_mt(int mt, const gemv::Args& a, cudaStream_t s, size_t smem) {
-  if (mt <= 1) return launch_one<BITS, CB, DQ, 1>(a, 0, s, smem);
-  if (mt <= 2) return launch_one<BITS, CB, DQ, 2>(a, 0, s, smem);
-  return launch_one<BITS, CB, DQ, 4>(a, 0, s, smem);
+int launch_seg(int seg, const gemv::Args& a, cudaStream_t s, size_t smem) {
+  if (seg == 1) return launch_one<BITS, CB, DQ, 1>(a, s, smem);
+  if (seg == 2) return launch_one<BITS, CB, DQ, 2>(a, s, smem);
+  return launch_one<BITS, CB, DQ, 4>(a, s, smem);
 }
 
 template <int BITS>
-int launch_bits(bool cb, bool dq, int mt, const gemv::Args& a, cudaStream_t s, size_t smem) {
-  if (cb) return dq ? launch_mt<BITS, true, true>(mt, a, s, smem) : launch_mt<BITS, true, false>(mt, a, s, smem);
-  return dq ? launch_mt<BITS, false, true>(mt, a, s, smem) : launch_mt<BITS, false, false>(mt, a, s, smem);
-}
-
-int pick_mt(int64_t tokens) {
-  return tokens <= 1 ? 1 : tokens <= 2 ? 2 : 4;
+int launch_bits(bool cb, bool dq, int seg, const gemv::Args& a, cudaStream_t s, size_t smem) {
+  if (cb) return dq ? launch_seg<BITS, true, true>(seg, a, s, smem) : launch_seg<BITS, true, false>(seg, a, s, smem);
+  return dq ? launch_seg<BITS, false, true>(seg, a, s, smem) : launch_seg<BITS, false, false>(seg, a, s, smem);
 }
 
 }  // namespace
 
-static int ilog2(int64_t v) {
-  int r = 0;
-  while ((int64_t(1) << (r + 1)) <= v) ++r;
-  return r;
-}
-
-// Whether the fast GEMV covers this weight layout.
+// Whether the tensor-core GEMV covers this weight layout: whole 16-byte
+// chunks per group (group bytes a power of two in [16, 2048]), a 16-byte row
+// pitch, and (double quantization) few enough super-groups per tile.
 bool gemv_supported(const ts_qweight& w) {
   const int64_t gbytes = (int64_t)w.group_size * w.bits / 8;
-  return (w.bits == 2 || w.bits == 4 || w.bits == 8) && gbytes % 16 == 0 &&
-         (gbytes & (gbytes - 1)) == 0 && w.rows * w.n_groups < (int64_t(1) << 31) &&
-         w.packed_row_bytes < (int64_t(1) << 30) &&
-         w.packed_row_bytes % 16 == 0 && is_aligned(w.packed, 16) &&
-         w.padded_cols % (128 / w.bits) == 0 && w.packed_row_bytes * 8 / w.bits >= w.padded_cols;
+  if (!(w.bits == 2 || w.bits == 4 || w.bits == 8) || gbytes < 16 || gbytes > gemv::kTileK ||
+      (gbytes & (gbytes - 1)) != 0)
+    return false;
+  if (w.rows * w.n_groups >= (int64_t(1) << 31) || w.packed_row_bytes >= (int64_t(1) << 30) ||
+      w.packed_row_bytes % 16 != 0 || !is_aligned(w.packed, 16) || w.packed_row_bytes * 8 / w.bits < w.padded_cols)
+    return false;
+  if (w.dq_scale_codes) {
+    const int64_t gpt = gemv::kTileK / gbytes;
+    if (15 * w.n_groups + gpt > (int64_t)(gemv::kMaxSupers - 2) * w.dq_group_size) return false;
+  }
+  return true;
 }
-
-static int gemv_grid_warps() { return sm_count() * 2 * gemv::kWarps; }
 
 size_t gemv_workspace_size(const ts_qweight& w) {
-  const int64_t rgs = (w.rows + gemv::kR - 1) / gemv::kR;
-  return align_up((size_t)rgs * sizeof(int), 256) +
-         (size_t)gemv_grid_warps() * 2 * gemv::kR * 4 * sizeof(float);
+  const int64_t rbs = (w.rows + gemv::kTileRows - 1) / gemv::kTileRows;
+  return align_up((size_t)rbs * sizeof(int), 256) + 256 +
+         (size_t)sm_count() * 2 * gemv::kTileRows * gemv::kMaxTok * sizeof(float);
 }
 
-static size_t gemv_smem(const ts_qweight& w, int mt) {
-  const int span = 128 / w.bits;
-  const int64_t chunk_w = 32 * span;
-  const int64_t n_chunks = (w.padded_cols + chunk_w - 1) / chunk_w;
-  size_t lut = w.codebook ? (w.bits == 2 ? 256 * 32 * 8 : 256 * 32 * 4) : 0;
-  return lut + (size_t)mt * n_chunks * chunk_w * 2 + (size_t)mt * n_chunks * 32 * sizeof(float2);
-}
-
-// Largest token count per pass whose staged activations fit in shared memory.
+// Largest token count per pass that fits shared memory with >= 2 stages.
 int gemv_max_tokens(const ts_qweight& w) {
-  const size_t cap = (size_t)std::min(max_smem_optin(), 200 * 1024);
-  for (int mt : {4, 2, 1})
-    if (gemv_smem(w, mt) <= cap) return mt;
+  const Plan p = make_plan(w);
+  for (int mt = gemv::kMaxTok; mt >= 1; --mt)
+    if (stages_for(w, p, mt) >= 2) return mt;
   return 0;
 }
 
@@ -629,8 +803,9 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   const int max_mt = gemv_max_tokens(w);
   TS_UNSUPPORTED(max_mt > 0, "qlinear: activations of %lld columns do not fit in shared memory",
                  (long long)w.cols);
-  TS_REQUIRE(ws_bytes >= gemv_workspace_size(w), "qlinear: workspace too small (%zu < %zu)",
-             ws_bytes, gemv_workspace_size(w));
+  TS_REQUIRE(ws_bytes >= gemv_workspace_size(w), "qlinear: workspace too small (%zu < %zu)", ws_bytes,
+             gemv_workspace_size(w));
+  const Plan p = make_plan(w);
   gemv::Args a;
   a.q = make_qw(w);
   a.x = x;
@@ -641,36 +816,53 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.out = out;
   a.out_dtype = out_dtype;
   a.out_stride = out_stride;
-  const int64_t rgs = (w.rows + gemv::kR - 1) / gemv::kR;
-  a.counters = reinterpret_cast<int*>(workspace);
-  a.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
-                                        align_up((size_t)rgs * sizeof(int), 256));
-  a.chunks = (uint32_t)((w.packed_row_bytes + 511) / 512);
-  a.units = (uint32_t)(rgs * a.chunks);
-  a.total_warps = (uint32_t)gemv_grid_warps();
-  const int64_t chunk_w = 32 * (128 / w.bits);
-  a.n_chunks_x = (int)((w.padded_cols + chunk_w - 1) / chunk_w);
-  a.center = w.bits == 4 ? 8.f : w.bits == 2 ? 2.f : 128.f;  // codebooks: set in-kernel
-  a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0;
+  const int64_t rbs = (w.rows + gemv::kTileRows - 1) / gemv::kTileRows;
+  char* ws = reinterpret_cast<char*>(workspace);
+  a.counters = reinterpret_cast<int*>(ws);
+  a.err = reinterpret_cast<int*>(ws + align_up((size_t)rbs * sizeof(int), 256));
+  a.partials = reinterpret_cast<float*>(ws + align_up((size_t)rbs * sizeof(int), 256) + 256);
+  a.tiles = p.tiles;
+  a.kgroups = p.kgroups;
+  a.grid = p.grid;
+  a.stage_bytes = p.stage_bytes;
+  a.meta_row_words = p.meta_row_words;
+  a.n_chunks = p.n_chunks;
+  a.seg_chunks = p.seg_chunks;
+  a.gpt = p.gpt;
+  a.max_owned_rows = p.max_owned_rows;
+  a.center = 0.f;  // uniform grids use raw codes; codebooks set their midpoint in-kernel
   a.gbytes_shift = ilog2((int64_t)w.group_size * w.bits / 8);
-  a.dq_shift = (w.dq_scale_codes && (w.dq_group_size & (w.dq_group_size - 1)) == 0)
-                   ? ilog2(w.dq_group_size) : -1;
+  const bool dq = w.dq_scale_codes != nullptr;
+  a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0;
+  {
+    const int step = dq ? 16 : 8;   // elements per 16 bytes of metadata
+    bool bulk = w.n_groups % step == 0 && p.gpt % step == 0;
+    if (dq) {
+      const int64_t n_sup = (w.rows * w.n_groups + w.dq_group_size - 1) / w.dq_group_size;
+      bulk = bulk && n_sup % 4 == 0 && is_aligned(w.dq_scale_codes, 16) && is_aligned(w.dq_gmin_codes, 16) &&
+             is_aligned(w.dq_scale_meta, 16) && is_aligned(w.dq_gmin_meta, 16);
+    } else {
+      bulk = bulk && is_aligned(w.scale, 16) && is_aligned(w.gmin, 16);
+    }
+    a.meta_bulk = bulk ? 1 : 0;
+  }
+  const bool cb = w.codebook != nullptr;
+  int rc = TS_OK;
   for (int64_t m0 = 0; m0 < M; m0 += max_mt) {
-    const int64_t tokens = std::min<int64_t>(max_mt, M - m0);
-    const int mt = pick_mt(tokens);
     a.m0 = m0;
-    a.mt = (int)tokens;
-    const size_t smem = gemv_smem(w, mt);
-    int rc;
+    a.mt = (int)std::min<int64_t>(max_mt, M - m0);
+    a.stages = stages_for(w, p, a.mt);
+    const size_t smem = fixed_smem(w, p, a.mt) + (size_t)a.stages * p.stage_bytes;
     if (w.bits == 4)
-      rc = launch_bits<4>(w.codebook != nullptr, w.dq_scale_codes != nullptr, mt, a, stream, smem);
+      rc = launch_bits<4>(cb, dq, p.seg_chunks, a, stream, smem);
     else if (w.bits == 2)
-      rc = launch_bits<2>(w.codebook != nullptr, w.dq_scale_codes != nullptr, mt, a, stream, smem);
+      rc = launch_bits<2>(cb, dq, p.seg_chunks, a, stream, smem);
     else
-      rc = launch_bits<8>(w.codebook != nullptr, w.dq_scale_codes != nullptr, mt, a, stream, smem);
+      rc = launch_bits<8>(cb, dq, p.seg_chunks, a, stream, smem);
     if (rc != TS_OK) return rc;
   }
   return TS_OK;
 }
 
 }  // namespace ts
+
