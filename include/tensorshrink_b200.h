@@ -100,6 +100,22 @@ TS_API int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M
                int out_dtype, int64_t out_row_stride, void* workspace,
                size_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free variant of ts_qlinear (no counterpart in the reference):
+ * same arguments minus the workspace. The decode kernel's scratch lives in a
+ * fixed per-device array of ts_qlinear_noalloc_max_scratch() bytes (256 KiB)
+ * inside the library, for callers that cannot allocate device memory. A
+ * weight whose ts_qlinear_workspace_size() exceeds that returns
+ * TS_ERR_UNSUPPORTED. The first call on each device resolves the array's
+ * address and must happen before any stream capture. Calls that may overlap
+ * on one device race on the shared array and must be serialized.
+ */
+TS_API size_t ts_qlinear_noalloc_max_scratch(void);
+
+TS_API int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtype, int64_t M,
+               int64_t x_row_stride, const void* bias, int bias_dtype, void* out,
+               int out_dtype, int64_t out_row_stride, void* stream);
+
 /* Standalone outlier correction into an fp32 result:
  *   out[m, row[k]] += x[m, col[k]] * delta[k]   for every k (any order).
  * Replaces triton_kernels.py:948-991 `apply_outlier_correction` (the path the

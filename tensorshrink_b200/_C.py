@@ -69,6 +69,9 @@ _SIGNATURES = [
     ("ts_qlinear_workspace_size", C.c_size_t, [C.POINTER(TsQWeight), _i64]),
     ("ts_qlinear", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int, _vp,
                              C.c_int, _i64, _vp, C.c_size_t, _vp]),
+    ("ts_qlinear_noalloc_max_scratch", C.c_size_t, []),
+    ("ts_qlinear_noalloc", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int,
+                                     _vp, C.c_int, _i64, _vp]),
     ("ts_apply_outlier_correction", C.c_int, [_vp, _i64, _i64, _i64, _vp, C.c_int, _i64, _vp, _vp,
                                               _vp, _i64, _vp]),
     ("ts_dequantize_weight", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, C.c_int, _vp]),

@@ -254,3 +254,61 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
 }
 
 }  // namespace ts
+
+// ---- allocation-free decode entry point -------------------------------------
+// Callers that may not allocate device memory at all (a serving loop replaying
+// pre-recorded work under a fixed memory budget, or a host whose allocator is
+// owned by another runtime and cannot be called from the decode thread) have
+// no place to put the fast decode kernel's split-row counters and partial
+// sums. This variant keeps them in a fixed per-device array compiled into the
+// library instead of a caller workspace. Module loading zero-fills the array;
+// every call that completes leaves the counters at zero again, which is the
+// state the next call needs. One array per device means two calls that may
+// overlap on the device (different streams, or different host threads) race
+// on it: serialize them.
+namespace ts {
+namespace {
+constexpr size_t kNoAllocScratchBytes = 256u << 10;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Address of this device's scratch array, resolved once per device with the
+// device current. The first call loads the module on that device, which a
+// stream capture does not allow: make it before capturing.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  TS_CUDA_TRY(cudaGetDevice(&dev));
+  TS_REQUIRE(dev >= 0 && dev < kMaxDevices, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    TS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TS_OK;
+}
+}  // namespace
+}  // namespace ts
+
+extern "C" size_t ts_qlinear_noalloc_max_scratch(void) { return ts::kNoAllocScratchBytes; }
+
+extern "C" int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtype, int64_t M,
+                                  int64_t x_row_stride, const void* bias, int bias_dtype, void* out,
+                                  int out_dtype, int64_t out_row_stride, void* stream) {
+  int rc = check_qweight(w);
+  if (rc != TS_OK) return rc;
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc != TS_OK) return rc;
+  const size_t need = gemv_supported(*w) ? gemv_workspace_size(*w) : 0;
+  TS_UNSUPPORTED(need <= kNoAllocScratchBytes,
+                 "ts_qlinear_noalloc: weight of %lld rows needs %zu bytes of scratch, above the "
+                 "fixed %zu; use ts_qlinear with a caller workspace",
+                 (long long)w->rows, need, kNoAllocScratchBytes);
+  return ts_qlinear(w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
+                    out_row_stride, scratch, kNoAllocScratchBytes, stream);
+}
