@@ -18,6 +18,12 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
 int run_generic_qlinear(const ts_qweight& w, const void* x, int x_dtype, int64_t M,
                         int64_t x_stride, const void* bias, int bias_dtype, void* out,
                         int out_dtype, int64_t out_stride, cudaStream_t stream);
+bool qgemm_supported(const ts_qweight& w, const void* x, int64_t x_stride);
+int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride, const void* bias,
+              int bias_dtype, void* out, int out_dtype, int64_t out_stride, cudaStream_t stream);
+// Token counts from this one up go to the tensor-core kernel (the GEMV
+// re-streams the weights once per 8 tokens).
+constexpr int64_t kQgemmMinTokens = 65;
 int run_dequant(const ts_qweight& w, void* out, int out_dtype, int64_t out_stride,
                 int apply_outliers, cudaStream_t stream);
 int run_outlier_atomic(float* out, int64_t M, int64_t out_stride, const void* x, int x_dtype,
@@ -130,6 +136,8 @@ int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M, int64
   TS_REQUIRE(w->n_outliers == 0 || w->outlier_row_ptr != nullptr,
              "qlinear needs the CSR outlier_row_ptr table");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (M >= kQgemmMinTokens && qgemm_supported(*w, x, x_row_stride))
+    return run_qgemm(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride, s);
   if (gemv_supported(*w)) {
     TS_REQUIRE(workspace != nullptr, "workspace is NULL (size %zu needed)", gemv_workspace_size(*w));
     return run_gemv(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
