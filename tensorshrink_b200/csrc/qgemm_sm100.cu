@@ -8,8 +8,9 @@
 // to a dense compute-dtype matrix, triton_kernels.py:1003-1186, then F.linear)
 // with one persistent kernel that never writes the dense matrix:
 //
-//   warp 0      TMA producer: x tiles [128 tokens x 64] (128B swizzle) and the
-//               packed code tile [BN rows x 64 columns] -> shared memory
+//   warp 0      TMA producer: x tiles [128 tokens x 64] (128B swizzle), the
+//               packed code tile [BN rows x 64 columns], and blocks of group
+//               metadata [BN rows x 16 bytes] -> shared memory
 //   warp 1      MMA issuer: owns the TMEM accumulators, one thread issues
 //               tcgen05.mma M=128 x N=BN x K=16 (4 per stage), commits to barriers
 //   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one token per
@@ -51,6 +52,8 @@ struct Args {
   int64_t out_stride;
   int mblocks, nblocks, kblocks;
   int stages;
+  int meta_tma;      // group metadata by TMA blocks (else per-thread loads)
+  int meta_groups;   // groups per metadata block (8 fp16 or 16 code bytes = 16 B)
 };
 
 template <int BN>
@@ -206,6 +209,7 @@ __device__ __forceinline__ float outlier_value(const QW& q, const float* cbs, in
 template <int BITS, bool CB, int XT, int BN>
 __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
+                 const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap gmap,
                  const Args a) {
   using C = Cfg<BN>;
   constexpr int kCodeBytes = kBK * BITS / 8;              // per weight row per stage
@@ -217,12 +221,16 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
   unsigned char* sA = smem;
   unsigned char* sB = smem + (size_t)S * kAStageBytes;
   unsigned char* sC = sB + (size_t)S * C::kBStageBytes;    // packed codes, [BN][kCodeBytes] per stage
-  uint64_t* ld_full = reinterpret_cast<uint64_t*>(sC + (size_t)S * kCStageBytes);
+  unsigned char* sM = sC + (size_t)S * kCStageBytes;     // 2 slots x {scale, min} x [BN][16 B]
+  constexpr int kMSlotBytes = 2 * BN * 16;
+  uint64_t* ld_full = reinterpret_cast<uint64_t*>(sM + 2 * kMSlotBytes);
   uint64_t* b_full = ld_full + S;
   uint64_t* empty = b_full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* m_full = tempty + 2;
+  uint64_t* m_empty = m_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m_empty + 2);
   float* cbs = reinterpret_cast<float*>(tmem_slot + 4);   // codebook copy (<= 256 floats)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -237,10 +245,16 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(tfull + i, 1);
       mbar_init(tempty + i, kEpiWarps * 32);
+      mbar_init(m_full + i, 1);
+      mbar_init(m_empty + i, C::kDqThreads);
     }
     fence_barrier_init();
     prefetch_tensormap(&xmap);
     prefetch_tensormap(&cmap);
+    if (a.meta_tma) {
+      prefetch_tensormap(&smap);
+      prefetch_tensormap(&gmap);
+    }
   }
   if (CB) {
     for (int i = threadIdx.x; i < (1 << BITS); i += blockDim.x) cbs[i] = q.codebook[i];
@@ -255,16 +269,27 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int ntiles = a.mblocks * a.nblocks;
   const int KB = a.kblocks;
+  // stages per metadata block (a block holds meta_groups consecutive groups)
+  const int spm = a.meta_groups * q.group_size / kBK;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t it = 0, mit = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const int m0 = (tile % a.mblocks) * kBM, n0 = (tile / a.mblocks) * BN;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % S;
+          if (a.meta_tma && kb % spm == 0) {
+            const int ms = mit & 1;
+            if (!mbar_wait_ns(m_empty + ms, ((mit >> 1) & 1) ^ 1, &g_err, 17)) { ok = false; break; }
+            mbar_arrive_expect_tx(m_full + ms, kMSlotBytes);
+            unsigned char* slot = sM + (size_t)ms * kMSlotBytes;
+            tma_load_2d(slot, &smap, (kb / spm) * a.meta_groups, n0, m_full + ms);
+            tma_load_2d(slot + BN * 16, &gmap, (kb / spm) * a.meta_groups, n0, m_full + ms);
+            ++mit;
+          }
           if (!mbar_wait_ns(empty + s, ((it / S) & 1) ^ 1, &g_err, 11)) { ok = false; break; }
           mbar_arrive_expect_tx(ld_full + s, kAStageBytes + kCStageBytes);
           tma_load_2d(sA + (size_t)s * kAStageBytes, &xmap, kb * kBK, m0, ld_full + s);
@@ -365,9 +390,10 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     const int gs = q.group_size;
     const bool dq = q.dqs_codes != nullptr;
     const int groups_per_stage = gs >= kBK ? 1 : kBK / gs;
-    // Group metadata is fetched two stages ahead (raw 16-bit scale/min, or the
-    // two double-quant code bytes) so its latency overlaps the conversion of
-    // the stages in between; the codes themselves arrive by TMA.
+    // Raw metadata of (row, group): 16-bit scale | 16-bit min << 16, or the
+    // two double-quant code bytes. From the TMA'd block in shared memory, or,
+    // when the metadata rows are not 16-byte multiples, loaded by this thread
+    // two stages ahead so the latency overlaps the stages in between.
     auto fetch = [&](int tile, int kb, uint32_t (&raw)[4]) {
       const int64_t row = (int64_t)(tile / a.mblocks) * BN + r;
       if (tile >= ntiles || row >= q.rows) return;
@@ -404,14 +430,18 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     uint32_t raw1[4] = {0, 0, 0, 0}, raw2[4] = {0, 0, 0, 0};
     int t2 = blockIdx.x, k2 = 1;                 // position of raw2 (raw1 = the current stage)
     if (k2 == KB) { k2 = 0; t2 += gridDim.x; }
-    fetch(blockIdx.x, 0, raw1);
-    fetch(t2, k2, raw2);
-    uint32_t it = 0;
+    if (!a.meta_tma) {
+      fetch(blockIdx.x, 0, raw1);
+      fetch(t2, k2, raw2);
+    }
+    uint32_t it = 0, mit = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const int64_t row = (int64_t)(tile / a.mblocks) * BN + r;
       const bool valid = row < q.rows;
-      // outliers of this row: cursor over column-sorted tables, full scan otherwise
+      // Outliers of this row. Column-sorted rows use a cursor whose next
+      // (column, delta) is loaded right after the previous patch, so it has
+      // landed by the stage that needs it; other rows scan their list.
       int o_beg = 0, o_end = 0;
       bool sorted = true;
       if (valid && q.n_outliers > 0) {
@@ -422,24 +452,50 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
       }
       int cur = o_beg;
       int next_col = cur < o_end ? q.ocol[cur] : INT_MAX;
+      float next_delta = cur < o_end ? __half2float(q.odelta[cur]) : 0.f;
 
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
         const int k0 = kb * kBK;
-        // rotate the metadata prefetch: raw1 -> current, fetch two ahead
-        const uint32_t rawc[4] = {raw1[0], raw1[1], raw1[2], raw1[3]};
+        uint32_t rawc[4] = {0, 0, 0, 0};
+        if (a.meta_tma) {
+          if (kb % spm == 0 &&
+              !mbar_wait_ns(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) { ok = false; break; }
+          const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + r * 16;
+          const int ib = (kb % spm) * kBK / gs;             // first group of this stage in the block
 #pragma unroll
-        for (int i2 = 0; i2 < 4; ++i2) raw1[i2] = raw2[i2];
-        if (++k2 == KB) { k2 = 0; t2 += gridDim.x; }
-        fetch(t2, k2, raw2);
+          for (int gi = 0; gi < 4; ++gi) {
+            if (gi < groups_per_stage) {
+              if (dq)
+                rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[BN * 16 + ib + gi] << 8);
+              else
+                rawc[gi] = (uint32_t)reinterpret_cast<const uint16_t*>(slot)[ib + gi] |
+                           ((uint32_t)reinterpret_cast<const uint16_t*>(slot + BN * 16)[ib + gi] << 16);
+            }
+          }
+          if (kb % spm == spm - 1 || kb == KB - 1) {
+            mbar_arrive(m_empty + (mit & 1));
+            ++mit;
+          }
+        } else {
+          // rotate the metadata prefetch: raw1 -> current, fetch two ahead
+#pragma unroll
+          for (int i2 = 0; i2 < 4; ++i2) {
+            rawc[i2] = raw1[i2];
+            raw1[i2] = raw2[i2];
+          }
+          if (++k2 == KB) { k2 = 0; t2 += gridDim.x; }
+          fetch(t2, k2, raw2);
+        }
         float2 sg[4];
         if (valid) decode(row, kb, rawc, sg);
 
         if (!mbar_wait_ns(empty + s, ((it / S) & 1) ^ 1, &g_err, 15) ||
             !mbar_wait_ns(ld_full + s, (it / S) & 1, &g_err, 16)) { ok = false; break; }
+        const unsigned char* crow = sC + (size_t)s * kCStageBytes + r * kCodeBytes;
         uint32_t cw[kCodeBytes / 4];
         {
-          const uint4* src = reinterpret_cast<const uint4*>(sC + (size_t)s * kCStageBytes + r * kCodeBytes);
+          const uint4* src = reinterpret_cast<const uint4*>(crow);
 #pragma unroll
           for (int i2 = 0; i2 < kCodeBytes / 16; ++i2) {
             const uint4 u = src[i2];
@@ -463,11 +519,20 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
           if (sorted) {
             while (next_col < k0 + kBK) {
               const int cc = next_col - k0;
-              const float val = outlier_value<CB>(q, cbs, row, next_col, cur);
+              const uint32_t byte = crow[cc * BITS / 8];
+              const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
+              const int gi = gs >= kBK ? 0 : cc / gs;
+              float2 g = sg[0];
+              if (gi == 1) g = sg[1];
+              if (gi == 2) g = sg[2];
+              if (gi == 3) g = sg[3];
+              const float v = CB ? cbs[code] : (float)code;
+              const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
               const uint32_t pv = pack2<XT>(val, val) & 0xFFFFu;
               *reinterpret_cast<uint16_t*>(brow + (((cc >> 3) ^ sw) << 4) + (cc & 7) * 2) = (uint16_t)pv;
               ++cur;
               next_col = cur < o_end ? q.ocol[cur] : INT_MAX;
+              next_delta = cur < o_end ? __half2float(q.odelta[cur]) : 0.f;
             }
           } else {
             for (int j = o_beg; j < o_end; ++j) {
@@ -500,7 +565,7 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 
 static size_t qgemm_smem(int BN, int bits, int S) {
   const size_t stage = qgemm::kAStageBytes + (size_t)BN * qgemm::kBK * 2 + (size_t)BN * qgemm::kBK * bits / 8;
-  return 1024 + (size_t)S * stage + (3 * S + 4) * 8 + 16 + 256 * 4;
+  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)BN * 16) + (3 * S + 8) * 8 + 16 + 256 * 4;
 }
 
 // Layout conditions of the tensor-core path (everything else uses the GEMV).
@@ -522,7 +587,7 @@ template <int BITS, bool CB, int XT, int BN>
 static int launch_qgemm(const CUtensorMap* maps, const qgemm::Args& a, int grid, size_t smem, cudaStream_t st) {
   auto k = qgemm::qgemm_kernel<BITS, CB, XT, BN>;
   TS_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<grid, qgemm::Cfg<BN>::kThreads, smem, st>>>(maps[0], maps[1], a);
+  k<<<grid, qgemm::Cfg<BN>::kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
   TS_LAUNCH_CHECK();
   return TS_OK;
 }
@@ -573,7 +638,7 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   const size_t smem = qgemm_smem(BN, w.bits, S);
   const int64_t ntiles = (int64_t)a.mblocks * a.nblocks;
   const int grid = (int)std::min<int64_t>(ntiles, sms);
-  CUtensorMap maps[2];
+  CUtensorMap maps[4];
   int rc = encode_tmap_2d(&maps[0], x, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)w.cols, (uint64_t)M,
                           (uint64_t)x_stride * 2, qgemm::kBK, qgemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TS_OK) return rc;
@@ -581,6 +646,29 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
                       (uint64_t)w.rows, (uint64_t)w.packed_row_bytes, qgemm::kBK * w.bits / 8, BN,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc != TS_OK) return rc;
+  // group metadata blocks of 16 bytes per row: 8 fp16 scales/mins, or 16
+  // double-quant code bytes; rows must be 16-byte multiples for the copies
+  const bool dq = w.dq_scale_codes != nullptr;
+  a.meta_groups = dq ? 16 : 8;
+  a.meta_tma = (w.n_groups % a.meta_groups == 0) &&
+               (int64_t)a.meta_groups * w.group_size % qgemm::kBK == 0 &&
+               (dq ? is_aligned(w.dq_scale_codes, 16) && is_aligned(w.dq_gmin_codes, 16)
+                   : is_aligned(w.scale, 16) && is_aligned(w.gmin, 16));
+  maps[2] = maps[0];
+  maps[3] = maps[0];
+  if (a.meta_tma) {
+    const CUtensorMapDataType t = dq ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const uint64_t eb = dq ? 1 : 2;
+    rc = encode_tmap_2d(&maps[2], dq ? (const void*)w.dq_scale_codes : w.scale, t, (uint64_t)w.n_groups,
+                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, a.meta_groups, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TS_OK) return rc;
+    rc = encode_tmap_2d(&maps[3], dq ? (const void*)w.dq_gmin_codes : w.gmin, t, (uint64_t)w.n_groups,
+                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, a.meta_groups, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TS_OK) return rc;
+  } else {
+    a.meta_groups = 1;   // unused; keeps the stages-per-block arithmetic nonzero
+    if ((int64_t)w.group_size < qgemm::kBK) a.meta_groups = qgemm::kBK / w.group_size;
+  }
   const bool cb = w.codebook != nullptr;
   const int xt = x_dtype == TS_BF16 ? 1 : 0;
   if (w.bits == 2) return launch_bits<2>(cb, xt, BN, maps, a, grid, smem, stream);
