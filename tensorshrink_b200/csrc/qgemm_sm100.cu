@@ -6,41 +6,48 @@
 //
 // Replaces the reference's M > 64 path (modules.py:898-922: dequantize_weight
 // to a dense compute-dtype matrix, triton_kernels.py:1003-1186, then F.linear)
-// with one persistent kernel that never writes the dense matrix:
+// with one persistent kernel that never writes the dense matrix. A tile is
+// 128 weight rows x BT tokens; the MMA computes D[weight row, token] with the
+// dequantized weights as the A operand in tensor memory and the activations
+// as the B operand in shared memory:
 //
-//   warp 0      TMA producer: x tiles [128 tokens x 64] (128B swizzle), the
-//               packed code tile [BN rows x 64 columns], and blocks of group
-//               metadata [BN rows x 16 bytes] -> shared memory
-//   warp 1      MMA issuer: owns the TMEM accumulators, one thread issues
-//               tcgen05.mma M=128 x N=BN x K=16 (4 per stage), commits to barriers
-//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one token per
-//               thread), + bias, convert, store
-//   warps 6..   dequantizers: one weight row per thread; each stage unpacks that
-//               row's 64 codes straight into the tensor-core operand layout
-//               (K-major, 128-byte swizzle) in the activation dtype, and patches
-//               the row's outliers in place as fp32(base + delta) rounded once,
-//               so the sparse correction costs no extra pass and no atomics.
+//   warp 0      TMA producer: activation tile [BT tokens x 64] (128B swizzle),
+//               packed code tile [128 rows x 64 columns], and blocks of group
+//               metadata [128 rows x 16 bytes] -> shared memory
+//   warp 1      MMA issuer: one thread issues tcgen05.mma M=128 x N=BT x K=16
+//               (4 per stage) from TMEM (A) and shared memory (B)
+//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one weight row per
+//               thread, 32 tokens per load), + bias, convert, coalesced stores
+//   warps 6-21  dequantizers, two groups taking alternate stages (a stage's
+//               conversion is one long dependent chain per thread, so two
+//               groups keep twice the work in flight): two threads per weight
+//               row, 32 columns each per stage, unpack codes to the activation
+//               dtype in registers, patch the row's outliers in place as
+//               fp32(base + delta) rounded once, and store the result into the
+//               stage's TMEM columns.
 //
-// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the
-// main loop of tile i+1. Every wait is bounded in wall-clock time: on timeout
-// the kernel records an error flag and all roles unwind to the final barrier,
-// where the TMEM is freed.
+// Keeping the dequantized tile out of shared memory leaves shared-memory
+// bandwidth to the activation operand alone (the tensor core reads A from
+// TMEM), which is what bounds a design that stages both operands there.
+// Every wait is bounded in wall-clock time: on timeout the kernel records an
+// error flag and all roles unwind to the final barrier, where the TMEM is freed.
 #include "sm100.cuh"
 
 namespace ts {
 namespace qgemm {
 
-constexpr int kBM = 128;        // tokens per tile = UMMA M
+constexpr int kBW = 128;        // weight rows per tile = UMMA M = TMEM lanes
 constexpr int kBK = 64;         // K per stage = one 128-byte swizzle row of 16-bit values
 constexpr int kEpiWarps = 4;
+constexpr int kDqGroups = 2;    // dequantizer groups, taking alternate stages
+constexpr int kDqGroupWarps = 8;  // per group: two per TMEM lane quadrant (one per half row)
+constexpr int kDqWarps = kDqGroups * kDqGroupWarps;
 constexpr int kFirstDqWarp = 2 + kEpiWarps;
-constexpr int kAStageBytes = kBM * kBK * 2;
+constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
+constexpr int kTmemCols = 512;
+constexpr int kAStageCols = kBK / 2;   // 64 16-bit values per lane = 32 columns
 
 __device__ int g_err;           // wait-timeout flag (diagnostic)
-
-__device__ __forceinline__ bool is_aligned_dev(const void* p, int a) {
-  return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(a - 1)) == 0;
-}
 
 struct Args {
   QW q;
@@ -50,18 +57,12 @@ struct Args {
   void* out;
   int out_dtype;
   int64_t out_stride;
-  int mblocks, nblocks, kblocks;
+  int tblocks, wblocks, kblocks;   // token blocks, weight-row blocks, stages per tile
   int stages;
   int meta_tma;      // group metadata by TMA blocks (else per-thread loads)
   int meta_groups;   // groups per metadata block (8 fp16 or 16 code bytes = 16 B)
-};
-
-template <int BN>
-struct Cfg {
-  static constexpr int kDqThreads = BN;                       // one weight row per thread
-  static constexpr int kThreads = (kFirstDqWarp * 32) + kDqThreads;
-  static constexpr int kBStageBytes = BN * kBK * 2;
-  static constexpr int kTmemCols = 2 * BN;
+  int gs_shift;      // log2(group_size)
+  int dq_shift;      // log2(dq_group_size), or -1 when it is not a power of two
 };
 
 // ---- dequantization of 8-column chunks ----------------------------------------
@@ -153,12 +154,12 @@ __device__ __forceinline__ uint4 dq_generic(const uint32_t* cw, const float* cbs
   return make_uint4(pack2<XT>(v[0], v[1]), pack2<XT>(v[2], v[3]), pack2<XT>(v[4], v[5]), pack2<XT>(v[6], v[7]));
 }
 
-// One weight row's 64 columns of a stage -> the swizzled operand row `brow`
-// (16-byte chunk j stored at chunk position j ^ sw). G = groups per stage,
+// 32 columns (one dequantizer's half of a stage row) -> 16 words of two
+// 16-bit values. G = groups in those 32 columns (1, or 2 for 16-column groups),
 // a compile-time constant so every per-group register is statically indexed.
 template <int BITS, bool CB, int XT, int G>
-__device__ __forceinline__ void convert_stage(const uint32_t* cw, const float2 (&sg)[4], const float* cbs,
-                                              unsigned char* brow, int sw) {
+__device__ __forceinline__ void convert_half(const uint32_t* cw, const float2 (&sg)[2], const float* cbs,
+                                             uint32_t (&wv)[16]) {
   if (BITS == 2) {
     uint32_t L0[G], L1[G];
 #pragma unroll
@@ -170,12 +171,12 @@ __device__ __forceinline__ void convert_stage(const uint32_t* cw, const float2 (
       L1[gi] = pack2<XT>(lv[2], lv[3]);
     }
 #pragma unroll
-    for (int wi = 0; wi < 4; ++wi) {
-      const int gi = wi * G / 4;
+    for (int wi = 0; wi < 2; ++wi) {
+      const int gi = wi * G / 2;
       uint4 c0, c1;
       dq2_lut(cw[wi], L0[gi], L1[gi], c0, c1);
-      *reinterpret_cast<uint4*>(brow + (((2 * wi) ^ sw) << 4)) = c0;
-      *reinterpret_cast<uint4*>(brow + (((2 * wi + 1) ^ sw) << 4)) = c1;
+      wv[8 * wi + 0] = c0.x; wv[8 * wi + 1] = c0.y; wv[8 * wi + 2] = c0.z; wv[8 * wi + 3] = c0.w;
+      wv[8 * wi + 4] = c1.x; wv[8 * wi + 5] = c1.y; wv[8 * wi + 6] = c1.z; wv[8 * wi + 7] = c1.w;
     }
   } else if (BITS == 4 && !CB) {
     uint32_t s2[G], g2[G];
@@ -186,14 +187,27 @@ __device__ __forceinline__ void convert_stage(const uint32_t* cw, const float2 (
       g2[gi] = pack2<XT>(gc, gc);
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<uint4*>(brow + ((j ^ sw) << 4)) = dq4_uniform<XT>(cw[j], s2[j * G / 8], g2[j * G / 8]);
+    for (int j = 0; j < 4; ++j) {
+      const uint4 c = dq4_uniform<XT>(cw[j], s2[j * G / 4], g2[j * G / 4]);
+      wv[4 * j + 0] = c.x; wv[4 * j + 1] = c.y; wv[4 * j + 2] = c.z; wv[4 * j + 3] = c.w;
+    }
   } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<uint4*>(brow + ((j ^ sw) << 4)) =
-          dq_generic<BITS, CB, XT>(&cw[j * BITS / 4], cbs, sg[j * G / 8].x, sg[j * G / 8].y);
+    for (int j = 0; j < 4; ++j) {
+      const uint4 c = dq_generic<BITS, CB, XT>(&cw[j * BITS / 4], cbs, sg[j * G / 4].x, sg[j * G / 4].y);
+      wv[4 * j + 0] = c.x; wv[4 * j + 1] = c.y; wv[4 * j + 2] = c.z; wv[4 * j + 3] = c.w;
+    }
   }
+}
+
+// Replace the 16-bit value at column cc (0..31) of the 16-word half row.
+__device__ __forceinline__ void patch_half(uint32_t (&wv)[16], int cc, uint32_t bits16) {
+  const int wi = cc >> 1;
+  const uint32_t keep = (cc & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+  const uint32_t put = (cc & 1) ? (bits16 << 16) : bits16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i == wi) wv[i] = (wv[i] & keep) | put;
 }
 
 // fp32 weight at an outlier position: base reconstruction + stored delta.
@@ -206,29 +220,29 @@ __device__ __forceinline__ float outlier_value(const QW& q, const float* cbs, in
 }
 
 // ---- the kernel -------------------------------------------------------------
-template <int BITS, bool CB, int XT, int BN>
-__global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
+template <int BITS, bool CB, int XT, int BT>
+__global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
                  const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap gmap,
                  const Args a) {
-  using C = Cfg<BN>;
+  constexpr int kXStageBytes = BT * kBK * 2;
   constexpr int kCodeBytes = kBK * BITS / 8;              // per weight row per stage
-  constexpr int kCStageBytes = BN * kCodeBytes;
+  constexpr int kCStageBytes = kBW * kCodeBytes;
+  constexpr int kMSlotBytes = 2 * kBW * 16;               // {scale, min} x [128 rows][16 B]
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base by pointer arithmetic on the shared array itself, so
+  // the compiler keeps the shared address space (ld.shared, not generic loads)
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int S = a.stages;
-  unsigned char* sA = smem;
-  unsigned char* sB = smem + (size_t)S * kAStageBytes;
-  unsigned char* sC = sB + (size_t)S * C::kBStageBytes;    // packed codes, [BN][kCodeBytes] per stage
-  unsigned char* sM = sC + (size_t)S * kCStageBytes;     // 2 slots x {scale, min} x [BN][16 B]
-  constexpr int kMSlotBytes = 2 * BN * 16;
+  unsigned char* sX = smem;
+  unsigned char* sC = sX + (size_t)S * kXStageBytes;
+  unsigned char* sM = sC + (size_t)S * kCStageBytes;
   uint64_t* ld_full = reinterpret_cast<uint64_t*>(sM + 2 * kMSlotBytes);
-  uint64_t* b_full = ld_full + S;
-  uint64_t* empty = b_full + S;
+  uint64_t* a_full = ld_full + S;
+  uint64_t* empty = a_full + S;
   uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* m_full = tempty + 2;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* m_full = tempty + 1;
   uint64_t* m_empty = m_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m_empty + 2);
   float* cbs = reinterpret_cast<float*>(tmem_slot + 4);   // codebook copy (<= 256 floats)
@@ -239,14 +253,14 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(ld_full + s, 1);
-      mbar_init(b_full + s, C::kDqThreads);
+      mbar_init(a_full + s, kDqGroupWarps);
       mbar_init(empty + s, 1);
     }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, kEpiWarps * 32);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(tfull + i, 1);
-      mbar_init(tempty + i, kEpiWarps * 32);
       mbar_init(m_full + i, 1);
-      mbar_init(m_empty + i, C::kDqThreads);
+      mbar_init(m_empty + i, kDqWarps);
     }
     fence_barrier_init();
     prefetch_tensormap(&xmap);
@@ -260,70 +274,73 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     for (int i = threadIdx.x; i < (1 << BITS); i += blockDim.x) cbs[i] = q.codebook[i];
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int ntiles = a.mblocks * a.nblocks;
+  const uint32_t tmem = *tmem_slot;         // columns [0, BT): accumulator; then S A-stages
+  const int ntiles = a.tblocks * a.wblocks;
   const int KB = a.kblocks;
-  // stages per metadata block (a block holds meta_groups consecutive groups)
-  const int spm = a.meta_groups * q.group_size / kBK;
+  const int spm = a.meta_groups * q.group_size / kBK;   // stages per metadata block
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      uint32_t it = 0, mit = 0;
+      uint32_t mit = 0, ph = 0;
+      int s = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % a.mblocks) * kBM, n0 = (tile / a.mblocks) * BN;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % S;
-          if (a.meta_tma && kb % spm == 0) {
+        const int m0 = (tile % a.tblocks) * BT, n0 = (tile / a.tblocks) * kBW;
+        for (int kb = 0, mk = 0; kb < KB; ++kb) {
+          if (a.meta_tma && mk == 0) {
             const int ms = mit & 1;
-            if (!mbar_wait_ns(m_empty + ms, ((mit >> 1) & 1) ^ 1, &g_err, 17)) { ok = false; break; }
+            if (!mbar_wait_hint(m_empty + ms, ((mit >> 1) & 1) ^ 1, &g_err, 17)) { ok = false; break; }
             mbar_arrive_expect_tx(m_full + ms, kMSlotBytes);
             unsigned char* slot = sM + (size_t)ms * kMSlotBytes;
             tma_load_2d(slot, &smap, (kb / spm) * a.meta_groups, n0, m_full + ms);
-            tma_load_2d(slot + BN * 16, &gmap, (kb / spm) * a.meta_groups, n0, m_full + ms);
+            tma_load_2d(slot + kBW * 16, &gmap, (kb / spm) * a.meta_groups, n0, m_full + ms);
             ++mit;
           }
-          if (!mbar_wait_ns(empty + s, ((it / S) & 1) ^ 1, &g_err, 11)) { ok = false; break; }
-          mbar_arrive_expect_tx(ld_full + s, kAStageBytes + kCStageBytes);
-          tma_load_2d(sA + (size_t)s * kAStageBytes, &xmap, kb * kBK, m0, ld_full + s);
+          if (!mbar_wait_hint(empty + s, ph ^ 1, &g_err, 11)) { ok = false; break; }
+          mbar_arrive_expect_tx(ld_full + s, kXStageBytes + kCStageBytes);
+          tma_load_2d(sX + (size_t)s * kXStageBytes, &xmap, kb * kBK, m0, ld_full + s);
           tma_load_2d(sC + (size_t)s * kCStageBytes, &cmap, kb * kCodeBytes, n0, ld_full + s);
+          if (++s == S) { s = 0; ph ^= 1; }
+          if (++mk == spm) mk = 0;
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    constexpr uint32_t idesc = umma_idesc_f16(XT, kBM, BN);
-    uint32_t it = 0;
+    constexpr uint32_t idesc = umma_idesc_f16(XT, kBW, BT);
+    uint32_t ph = 0;
+    int s = 0;
     bool ok = true;
     int t_local = 0;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t_local) {
-      const int acc = t_local & 1;
-      if (!mbar_wait_ns(tempty + acc, ((t_local >> 1) & 1) ^ 1, &g_err, 12)) { ok = false; break; }
+      if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t d = tmem + acc * BN;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % S;
-        if (!mbar_wait_ns(ld_full + s, (it / S) & 1, &g_err, 13) ||
-            !mbar_wait_ns(b_full + s, (it / S) & 1, &g_err, 13)) { ok = false; break; }
+      for (int kb = 0; kb < KB; ++kb) {
+        // one lane waits, the warp follows
+        int w_ok = 1;
+        if (lane == 0)
+          w_ok = mbar_wait_hint(ld_full + s, ph, &g_err, 13) && mbar_wait_hint(a_full + s, ph, &g_err, 13);
+        if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
-          const uint64_t ad = umma_desc_sw128(smem_u32(sA + (size_t)s * kAStageBytes));
-          const uint64_t bd = umma_desc_sw128(smem_u32(sB + (size_t)s * C::kBStageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(sX + (size_t)s * kXStageBytes));
+          const uint32_t at = tmem + BT + s * kAStageCols;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)   // +32 bytes along K per step = +2 in the 16-byte address field
-            umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < kBK / 16; ++k)   // K=16: 8 TMEM columns of A, +32 bytes of B (+2 in the address field)
+            umma_f16_ts(tmem, at + 8 * k, bd + 2 * k, idesc, (kb | k) != 0);
           umma_commit(empty + s);
         }
         __syncwarp();
+        if (++s == S) { s = 0; ph ^= 1; }
       }
-      if (lane == 0) umma_commit(tfull + acc);
+      if (lane == 0) umma_commit(tfull);
       __syncwarp();
     }
   } else if (warp < kFirstDqWarp) {
@@ -331,76 +348,61 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     const int quad = warp & 3;                      // TMEM lanes this warp may read
     int t_local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
-      const int acc = t_local & 1;
-      const int m0 = (tile % a.mblocks) * kBM, n0 = (tile / a.mblocks) * BN;
-      if (!mbar_wait_ns(tfull + acc, (t_local >> 1) & 1, &g_err, 14)) break;
+      const int64_t m0 = (int64_t)(tile % a.tblocks) * BT;
+      const int64_t n = (int64_t)(tile / a.tblocks) * kBW + quad * 32 + lane;   // this thread's weight row
+      if (!mbar_wait_hint(tfull, t_local & 1, &g_err, 14)) break;
       tc_fence_after();
-      const int64_t m = m0 + quad * 32 + lane;
-      const bool mvalid = m < a.M;
+      const bool nvalid = n < q.rows;
+      const float bias = (a.bias && nvalid) ? load_f(a.bias, a.bias_dtype, n) : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < BT / 32; ++c) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, v);
-        const int64_t nb = n0 + c * 32;
-        if (a.bias) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (nb + i < q.rows) v[i] += load_f(a.bias, a.bias_dtype, nb + i);
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c * 32, v);
+        if (c == BT / 32 - 1) {
+          // accumulator fully read: the MMA may start the next tile
+          tc_fence_before();
+          mbar_arrive(tempty);
         }
-        if (mvalid) {
-          const int64_t o = m * a.out_stride + nb;
-          const bool full_vec = nb + 32 <= q.rows;
-          if (a.out_dtype == TS_F32) {
-            float* op = reinterpret_cast<float*>(a.out) + o;
-            if (full_vec && is_aligned_dev(op, 16)) {
+        if (!nvalid) continue;
+        const int64_t mb = m0 + c * 32;
+        const int jn = a.M - mb < 32 ? (int)(a.M - mb) : 32;
+        if (a.out_dtype == TS_F32) {
+          float* op = reinterpret_cast<float*>(a.out) + mb * a.out_stride + n;
 #pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(op + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-            } else {
-              for (int i = 0; i < 32; ++i)
-                if (nb + i < q.rows) op[i] = v[i];
-            }
-          } else {
-            uint16_t* op = reinterpret_cast<uint16_t*>(a.out) + o;
-            if (full_vec && is_aligned_dev(op, 16)) {
+          for (int j = 0; j < 32; ++j)
+            if (j < jn) op[j * a.out_stride] = v[j] + bias;
+        } else if (a.out_dtype == TS_BF16) {
+          __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + mb * a.out_stride + n;
 #pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 w;
-                if (a.out_dtype == TS_BF16)
-                  w = make_uint4(pack2<1>(v[i], v[i + 1]), pack2<1>(v[i + 2], v[i + 3]),
-                                 pack2<1>(v[i + 4], v[i + 5]), pack2<1>(v[i + 6], v[i + 7]));
-                else
-                  w = make_uint4(pack2<0>(v[i], v[i + 1]), pack2<0>(v[i + 2], v[i + 3]),
-                                 pack2<0>(v[i + 4], v[i + 5]), pack2<0>(v[i + 6], v[i + 7]));
-                *reinterpret_cast<uint4*>(op + i) = w;
-              }
-            } else {
-              for (int i = 0; i < 32; ++i)
-                if (nb + i < q.rows) store_f(a.out, a.out_dtype, o + i, v[i]);
-            }
-          }
+          for (int j = 0; j < 32; ++j)
+            if (j < jn) op[j * a.out_stride] = __float2bfloat16_rn(v[j] + bias);
+        } else {
+          __half* op = reinterpret_cast<__half*>(a.out) + mb * a.out_stride + n;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < jn) op[j * a.out_stride] = __float2half_rn(v[j] + bias);
         }
       }
-      tc_fence_before();
-      mbar_arrive(tempty + acc);
     }
   } else {
     // ---------------- dequantizers ----------------
-    const int r = threadIdx.x - kFirstDqWarp * 32;      // tile row of this thread
+    const int quad = warp & 3;
+    const int half = ((warp - kFirstDqWarp) >> 2) & 1;   // columns [32 half, 32 half + 32) of a stage
+    const int grp = (warp - kFirstDqWarp) / kDqGroupWarps; // this group converts stages with kb % 2 == grp
+    const int rl = quad * 32 + lane;                      // tile row of this thread = TMEM lane
     const int gs = q.group_size;
     const bool dq = q.dqs_codes != nullptr;
-    const int groups_per_stage = gs >= kBK ? 1 : kBK / gs;
+    const int gph = gs >= 32 ? 1 : 32 / gs;               // groups in this thread's 32 columns (1 or 2)
     // Raw metadata of (row, group): 16-bit scale | 16-bit min << 16, or the
     // two double-quant code bytes. From the TMA'd block in shared memory, or,
-    // when the metadata rows are not 16-byte multiples, loaded by this thread
-    // two stages ahead so the latency overlaps the stages in between.
-    auto fetch = [&](int tile, int kb, uint32_t (&raw)[4]) {
-      const int64_t row = (int64_t)(tile / a.mblocks) * BN + r;
+    // when the metadata rows are not 16-byte multiples, loaded by this thread.
+    auto fetch = [&](int tile, int kb, uint32_t (&raw)[2]) {
+      const int64_t row = (int64_t)(tile / a.tblocks) * kBW + rl;
       if (tile >= ntiles || row >= q.rows) return;
-      const int64_t flat = row * q.n_groups + (int64_t)kb * kBK / gs;
+      const int64_t flat = row * q.n_groups + ((kb * kBK + 32 * half) >> a.gs_shift);
 #pragma unroll
-      for (int gi = 0; gi < 4; ++gi) {
-        if (gi < groups_per_stage) {
+      for (int gi = 0; gi < 2; ++gi) {
+        if (gi < gph) {
           if (dq)
             raw[gi] = (uint32_t)__ldg(q.dqs_codes + flat + gi) | ((uint32_t)__ldg(q.dqg_codes + flat + gi) << 8);
           else
@@ -409,13 +411,13 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
         }
       }
     };
-    auto decode = [&](int64_t row, int kb, const uint32_t (&raw)[4], float2 (&sg)[4]) {
-      const int64_t flat = row * q.n_groups + (int64_t)kb * kBK / gs;
+    auto decode = [&](int64_t row, int kb, const uint32_t (&raw)[2], float2 (&sg)[2]) {
+      const int64_t flat = row * q.n_groups + ((kb * kBK + 32 * half) >> a.gs_shift);
 #pragma unroll
-      for (int gi = 0; gi < 4; ++gi) {
-        if (gi < groups_per_stage) {
+      for (int gi = 0; gi < 2; ++gi) {
+        if (gi < gph) {
           if (dq) {
-            const int64_t sup = (flat + gi) / q.dq_gs;
+            const int64_t sup = a.dq_shift >= 0 ? (flat + gi) >> a.dq_shift : (flat + gi) / q.dq_gs;
             const float2 ms = __half22float2(q.dqs_meta[sup]);
             const float2 mg = __half22float2(q.dqg_meta[sup]);
             sg[gi].x = __fadd_rn(__fmul_rn((float)(raw[gi] & 0xFF), ms.x), ms.y);
@@ -427,17 +429,12 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
         }
       }
     };
-    uint32_t raw1[4] = {0, 0, 0, 0}, raw2[4] = {0, 0, 0, 0};
-    int t2 = blockIdx.x, k2 = 1;                 // position of raw2 (raw1 = the current stage)
-    if (k2 == KB) { k2 = 0; t2 += gridDim.x; }
-    if (!a.meta_tma) {
-      fetch(blockIdx.x, 0, raw1);
-      fetch(t2, k2, raw2);
-    }
-    uint32_t it = 0, mit = 0;
+    uint32_t mit = 0, ph = 0;
+    int s = 0;
     bool ok = true;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + BT + half * (kAStageCols / 2);
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const int64_t row = (int64_t)(tile / a.mblocks) * BN + r;
+      const int64_t row = (int64_t)(tile / a.tblocks) * kBW + rl;
       const bool valid = row < q.rows;
       // Outliers of this row. Column-sorted rows use a cursor whose next
       // (column, delta) is loaded right after the previous patch, so it has
@@ -450,103 +447,118 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
         for (int j = o_beg + 1; j < o_end; ++j)
           if (q.ocol[j] < q.ocol[j - 1]) { sorted = false; break; }
       }
+      // the cursor skips outliers in the other thread's half and the other
+      // group's stages
       int cur = o_beg;
-      int next_col = cur < o_end ? q.ocol[cur] : INT_MAX;
-      float next_delta = cur < o_end ? __half2float(q.odelta[cur]) : 0.f;
+      int next_col = INT_MAX;
+      float next_delta = 0.f;
+      auto advance = [&]() {
+        next_col = INT_MAX;
+        while (cur < o_end) {
+          const int c = q.ocol[cur];
+          if (((c >> 5) & 1) == half && ((c >> 6) & 1) == grp) {
+            next_col = c;
+            next_delta = __half2float(q.odelta[cur]);
+            break;
+          }
+          ++cur;
+        }
+      };
+      if (sorted) advance();
 
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % S;
-        const int k0 = kb * kBK;
-        uint32_t rawc[4] = {0, 0, 0, 0};
+      for (int kb = 0, mk = 0; kb < KB; ++kb) {
+        // stage slot and phase of this kb, then advance the counters for the next
+        const int cs = s;
+        const uint32_t cph = ph;
+        if (++s == S) { s = 0; ph ^= 1; }
+        const int cmk = mk;
+        if (++mk == spm) mk = 0;
+        const int c0 = kb * kBK + 32 * half;               // first column of this thread's half
+        const bool mine = (kb & 1) == grp;
+        uint32_t rawc[2] = {0, 0};
         if (a.meta_tma) {
-          if (kb % spm == 0 &&
-              !mbar_wait_ns(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) { ok = false; break; }
-          const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + r * 16;
-          const int ib = (kb % spm) * kBK / gs;             // first group of this stage in the block
+          // Both groups wait for every metadata block and release it at its
+          // end, so a release can never be counted toward an older use of
+          // the slot.
+          if (cmk == 0 &&
+              !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) { ok = false; break; }
+          const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
+          const int ib = ((cmk << 6) + 32 * half) >> a.gs_shift;   // group of c0 within the block
 #pragma unroll
-          for (int gi = 0; gi < 4; ++gi) {
-            if (gi < groups_per_stage) {
+          for (int gi = 0; gi < 2; ++gi) {
+            if (mine && gi < gph) {
               if (dq)
-                rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[BN * 16 + ib + gi] << 8);
+                rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[kBW * 16 + ib + gi] << 8);
               else
                 rawc[gi] = (uint32_t)reinterpret_cast<const uint16_t*>(slot)[ib + gi] |
-                           ((uint32_t)reinterpret_cast<const uint16_t*>(slot + BN * 16)[ib + gi] << 16);
+                           ((uint32_t)reinterpret_cast<const uint16_t*>(slot + kBW * 16)[ib + gi] << 16);
             }
           }
-          if (kb % spm == spm - 1 || kb == KB - 1) {
-            mbar_arrive(m_empty + (mit & 1));
+          if (cmk == spm - 1 || kb == KB - 1) {
+            // one arrival per warp: 256 arrivals on one barrier word would
+            // serialize in the shared-memory atomic unit every stage
+            __syncwarp();
+            if (lane == 0) mbar_arrive(m_empty + (mit & 1));
             ++mit;
           }
-        } else {
-          // rotate the metadata prefetch: raw1 -> current, fetch two ahead
-#pragma unroll
-          for (int i2 = 0; i2 < 4; ++i2) {
-            rawc[i2] = raw1[i2];
-            raw1[i2] = raw2[i2];
-          }
-          if (++k2 == KB) { k2 = 0; t2 += gridDim.x; }
-          fetch(t2, k2, raw2);
+        } else if (mine) {
+          fetch(tile, kb, rawc);
         }
-        float2 sg[4];
+        if (!mine) continue;
+        float2 sg[2];
         if (valid) decode(row, kb, rawc, sg);
 
-        if (!mbar_wait_ns(empty + s, ((it / S) & 1) ^ 1, &g_err, 15) ||
-            !mbar_wait_ns(ld_full + s, (it / S) & 1, &g_err, 16)) { ok = false; break; }
-        const unsigned char* crow = sC + (size_t)s * kCStageBytes + r * kCodeBytes;
-        uint32_t cw[kCodeBytes / 4];
-        {
-          const uint4* src = reinterpret_cast<const uint4*>(crow);
+        if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15) ||
+            !mbar_wait_hint(ld_full + cs, cph, &g_err, 16)) { ok = false; break; }
+        const unsigned char* crow = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes + half * (kCodeBytes / 2);
+        uint32_t cw[kCodeBytes / 8];
+        if (kCodeBytes / 2 >= 16) {
 #pragma unroll
-          for (int i2 = 0; i2 < kCodeBytes / 16; ++i2) {
-            const uint4 u = src[i2];
+          for (int i2 = 0; i2 < kCodeBytes / 32; ++i2) {
+            const uint4 u = reinterpret_cast<const uint4*>(crow)[i2];
             cw[4 * i2] = u.x; cw[4 * i2 + 1] = u.y; cw[4 * i2 + 2] = u.z; cw[4 * i2 + 3] = u.w;
           }
+        } else {
+          const uint2 u = *reinterpret_cast<const uint2*>(crow);
+          cw[0] = u.x; cw[kCodeBytes / 8 - 1] = u.y;
         }
-        unsigned char* brow = sB + (size_t)s * C::kBStageBytes + r * 128;
-        const int sw = r & 7;
+        uint32_t wv[16];
         if (!valid) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(brow + ((j ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
-        } else if (groups_per_stage == 1) {
-          convert_stage<BITS, CB, XT, 1>(cw, sg, cbs, brow, sw);
-        } else if (groups_per_stage == 2) {
-          convert_stage<BITS, CB, XT, 2>(cw, sg, cbs, brow, sw);
+          for (int j = 0; j < 16; ++j) wv[j] = 0;
+        } else if (gph == 1) {
+          convert_half<BITS, CB, XT, 1>(cw, sg, cbs, wv);
         } else {
-          convert_stage<BITS, CB, XT, 4>(cw, sg, cbs, brow, sw);
+          convert_half<BITS, CB, XT, 2>(cw, sg, cbs, wv);
         }
-        // outliers in [k0, k0 + 64): value = fp32(base) + delta, rounded once
+        // outliers in this thread's 32 columns: value = fp32(base) + delta, rounded once
         if (valid && o_end > o_beg) {
           if (sorted) {
-            while (next_col < k0 + kBK) {
-              const int cc = next_col - k0;
+            while (next_col < c0 + 32) {
+              const int cc = next_col - c0;
               const uint32_t byte = crow[cc * BITS / 8];
               const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
-              const int gi = gs >= kBK ? 0 : cc / gs;
-              float2 g = sg[0];
-              if (gi == 1) g = sg[1];
-              if (gi == 2) g = sg[2];
-              if (gi == 3) g = sg[3];
+              const float2 g = (gph == 2 && cc >= 16) ? sg[1] : sg[0];
               const float v = CB ? cbs[code] : (float)code;
               const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
-              const uint32_t pv = pack2<XT>(val, val) & 0xFFFFu;
-              *reinterpret_cast<uint16_t*>(brow + (((cc >> 3) ^ sw) << 4) + (cc & 7) * 2) = (uint16_t)pv;
+              patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
               ++cur;
-              next_col = cur < o_end ? q.ocol[cur] : INT_MAX;
-              next_delta = cur < o_end ? __half2float(q.odelta[cur]) : 0.f;
+              advance();
             }
           } else {
             for (int j = o_beg; j < o_end; ++j) {
               const int c = q.ocol[j];
-              if (c < k0 || c >= k0 + kBK) continue;
-              const int cc = c - k0;
+              if (c < c0 || c >= c0 + 32) continue;
               const float val = outlier_value<CB>(q, cbs, row, c, j);
-              const uint32_t pv = pack2<XT>(val, val) & 0xFFFFu;
-              *reinterpret_cast<uint16_t*>(brow + (((cc >> 3) ^ sw) << 4) + (cc & 7) * 2) = (uint16_t)pv;
+              patch_half(wv, c - c0, pack2<XT>(val, val) & 0xFFFFu);
             }
           }
         }
-        fence_proxy_async_smem();
-        mbar_arrive(b_full + s);
+        tmem_st16(lane_base + cs * kAStageCols, wv);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full + cs);
       }
     }
   }
@@ -555,7 +567,7 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -563,50 +575,51 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 
 // ---- host -------------------------------------------------------------------
 
-static size_t qgemm_smem(int BN, int bits, int S) {
-  const size_t stage = qgemm::kAStageBytes + (size_t)BN * qgemm::kBK * 2 + (size_t)BN * qgemm::kBK * bits / 8;
-  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)BN * 16) + (3 * S + 8) * 8 + 16 + 256 * 4;
+static size_t qgemm_smem(int BT, int bits, int S) {
+  const size_t stage = (size_t)BT * qgemm::kBK * 2 + (size_t)qgemm::kBW * qgemm::kBK * bits / 8;
+  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 8) * 8 + 16 + 256 * 4;
 }
+
+static int max_stages(int BT) { return (qgemm::kTmemCols - BT) / qgemm::kAStageCols; }
 
 // Layout conditions of the tensor-core path (everything else uses the GEMV).
 bool qgemm_supported(const ts_qweight& w, const void* x, int64_t x_stride) {
   if (!(w.bits == 2 || w.bits == 4 || w.bits == 8)) return false;
   const int gs = w.group_size;
-  if (gs % 8 != 0 || !(gs % qgemm::kBK == 0 || qgemm::kBK % gs == 0)) return false;
-  if (gs < 16 && w.bits == 2) return false;
+  if (gs < 16 || (gs & (gs - 1)) != 0) return false;   // power-of-two groups of at least 16
   const int64_t kb = (w.cols + qgemm::kBK - 1) / qgemm::kBK;
   if (kb * qgemm::kBK > w.padded_cols || kb * qgemm::kBK * w.bits / 8 > w.packed_row_bytes) return false;
   if (w.packed_row_bytes % 16 != 0 || !is_aligned(w.packed, 16)) return false;
   if (w.rows * w.n_groups >= (int64_t(1) << 31) || w.rows >= (int64_t(1) << 31)) return false;
   if (!is_aligned(x, 16) || (x_stride * 2) % 16 != 0) return false;
   if (w.cols < 1) return false;
-  return max_smem_optin() >= (int)qgemm_smem(128, w.bits, 3);
+  return max_smem_optin() >= (int)qgemm_smem(256, w.bits, 2);
 }
 
-template <int BITS, bool CB, int XT, int BN>
+template <int BITS, bool CB, int XT, int BT>
 static int launch_qgemm(const CUtensorMap* maps, const qgemm::Args& a, int grid, size_t smem, cudaStream_t st) {
-  auto k = qgemm::qgemm_kernel<BITS, CB, XT, BN>;
+  auto k = qgemm::qgemm_kernel<BITS, CB, XT, BT>;
   TS_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<grid, qgemm::Cfg<BN>::kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
+  k<<<grid, qgemm::kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
   TS_LAUNCH_CHECK();
   return TS_OK;
 }
 
 template <int BITS, bool CB, int XT>
-static int launch_bn(int BN, const CUtensorMap* maps, const qgemm::Args& a, int grid, size_t smem,
+static int launch_bt(int BT, const CUtensorMap* maps, const qgemm::Args& a, int grid, size_t smem,
                      cudaStream_t st) {
-  if (BN == 256) return launch_qgemm<BITS, CB, XT, 256>(maps, a, grid, smem, st);
+  if (BT == 256) return launch_qgemm<BITS, CB, XT, 256>(maps, a, grid, smem, st);
   return launch_qgemm<BITS, CB, XT, 128>(maps, a, grid, smem, st);
 }
 
 template <int BITS>
-static int launch_bits(bool cb, int xt, int BN, const CUtensorMap* maps, const qgemm::Args& a, int grid,
+static int launch_bits(bool cb, int xt, int BT, const CUtensorMap* maps, const qgemm::Args& a, int grid,
                        size_t smem, cudaStream_t st) {
   if (cb)
-    return xt ? launch_bn<BITS, true, 1>(BN, maps, a, grid, smem, st)
-              : launch_bn<BITS, true, 0>(BN, maps, a, grid, smem, st);
-  return xt ? launch_bn<BITS, false, 1>(BN, maps, a, grid, smem, st)
-            : launch_bn<BITS, false, 0>(BN, maps, a, grid, smem, st);
+    return xt ? launch_bt<BITS, true, 1>(BT, maps, a, grid, smem, st)
+              : launch_bt<BITS, true, 0>(BT, maps, a, grid, smem, st);
+  return xt ? launch_bt<BITS, false, 1>(BT, maps, a, grid, smem, st)
+            : launch_bt<BITS, false, 0>(BT, maps, a, grid, smem, st);
 }
 
 int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride, const void* bias,
@@ -620,30 +633,26 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   a.out = out;
   a.out_dtype = out_dtype;
   a.out_stride = out_stride;
-  a.mblocks = (int)((M + qgemm::kBM - 1) / qgemm::kBM);
+  a.wblocks = (int)((w.rows + qgemm::kBW - 1) / qgemm::kBW);
   a.kblocks = (int)((w.cols + qgemm::kBK - 1) / qgemm::kBK);
   const int sms = sm_count();
-  // 256-row tiles unless that leaves most SMs idle or does not fit
-  int BN = 256;
-  if ((int64_t)a.mblocks * ((w.rows + 255) / 256) < sms) BN = 128;
-  int S = 8;
-  while (S > 2 && qgemm_smem(BN, w.bits, S) > (size_t)max_smem_optin()) --S;
-  if (S < 3 && BN == 256) {
-    BN = 128;
-    S = 8;
-    while (S > 2 && qgemm_smem(BN, w.bits, S) > (size_t)max_smem_optin()) --S;
-  }
-  a.nblocks = (int)((w.rows + BN - 1) / BN);
+  // 256-token tiles halve the dequantization per flop; 128-token tiles when
+  // 256 would leave SMs idle
+  int BT = 256;
+  if ((int64_t)((M + 255) / 256) * a.wblocks < sms) BT = 128;
+  a.tblocks = (int)((M + BT - 1) / BT);
+  int S = max_stages(BT);
+  while (S > 2 && qgemm_smem(BT, w.bits, S) > (size_t)max_smem_optin()) --S;
   a.stages = S;
-  const size_t smem = qgemm_smem(BN, w.bits, S);
-  const int64_t ntiles = (int64_t)a.mblocks * a.nblocks;
+  const size_t smem = qgemm_smem(BT, w.bits, S);
+  const int64_t ntiles = (int64_t)a.tblocks * a.wblocks;
   const int grid = (int)std::min<int64_t>(ntiles, sms);
   CUtensorMap maps[4];
   int rc = encode_tmap_2d(&maps[0], x, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)w.cols, (uint64_t)M,
-                          (uint64_t)x_stride * 2, qgemm::kBK, qgemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+                          (uint64_t)x_stride * 2, qgemm::kBK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TS_OK) return rc;
   rc = encode_tmap_2d(&maps[1], w.packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)w.packed_row_bytes,
-                      (uint64_t)w.rows, (uint64_t)w.packed_row_bytes, qgemm::kBK * w.bits / 8, BN,
+                      (uint64_t)w.rows, (uint64_t)w.packed_row_bytes, qgemm::kBK * w.bits / 8, qgemm::kBW,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc != TS_OK) return rc;
   // group metadata blocks of 16 bytes per row: 8 fp16 scales/mins, or 16
@@ -660,20 +669,28 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
     const CUtensorMapDataType t = dq ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
     const uint64_t eb = dq ? 1 : 2;
     rc = encode_tmap_2d(&maps[2], dq ? (const void*)w.dq_scale_codes : w.scale, t, (uint64_t)w.n_groups,
-                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, a.meta_groups, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, a.meta_groups, qgemm::kBW,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != TS_OK) return rc;
     rc = encode_tmap_2d(&maps[3], dq ? (const void*)w.dq_gmin_codes : w.gmin, t, (uint64_t)w.n_groups,
-                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, a.meta_groups, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, a.meta_groups, qgemm::kBW,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != TS_OK) return rc;
   } else {
-    a.meta_groups = 1;   // unused; keeps the stages-per-block arithmetic nonzero
-    if ((int64_t)w.group_size < qgemm::kBK) a.meta_groups = qgemm::kBK / w.group_size;
+    a.meta_groups = w.group_size >= qgemm::kBK ? 1 : qgemm::kBK / w.group_size;   // keeps spm >= 1 (unused)
+  }
+  a.gs_shift = 0;
+  while ((1 << a.gs_shift) < w.group_size) ++a.gs_shift;
+  a.dq_shift = -1;
+  if (w.dq_group_size > 0 && (w.dq_group_size & (w.dq_group_size - 1)) == 0) {
+    a.dq_shift = 0;
+    while ((1 << a.dq_shift) < w.dq_group_size) ++a.dq_shift;
   }
   const bool cb = w.codebook != nullptr;
   const int xt = x_dtype == TS_BF16 ? 1 : 0;
-  if (w.bits == 2) return launch_bits<2>(cb, xt, BN, maps, a, grid, smem, stream);
-  if (w.bits == 4) return launch_bits<4>(cb, xt, BN, maps, a, grid, smem, stream);
-  return launch_bits<8>(cb, xt, BN, maps, a, grid, smem, stream);
+  if (w.bits == 2) return launch_bits<2>(cb, xt, BT, maps, a, grid, smem, stream);
+  if (w.bits == 4) return launch_bits<4>(cb, xt, BT, maps, a, grid, smem, stream);
+  return launch_bits<8>(cb, xt, BT, maps, a, grid, smem, stream);
 }
 
 }  // namespace ts
