@@ -19,6 +19,10 @@ memory and the output copied back inside the timed region.
 Multi-GPU (torchrun, one process per GPU): each rank runs its own copy of the
 workload ("scaling": "weak"); time is the max over ranks.
 
+The same JSON line carries a `prefill` object: TFLOP/s of the BASELINE
+configs[2] layer ([8192, 8192], 2-bit Lloyd-Max g64, 0.1% outliers) at M=2048
+bf16 on the tensor-core kernel, each launch timed alone after an L2 flush.
+
 --impl reference times the reference algorithm's CPU path (the numpy port
 in oracle/, on all host threads) on a bounded sample of the same workload.
 """
@@ -41,6 +45,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "QuantLinear packed-weight HBM GB/s (M=1) & TFLOP/s (M=2048); decode tok/s"
 HIDDEN, INTER = 4096, 14336
+# DRAM bytes per launch (read + write) measured by ncu on this workload
+QGEMV_TRAFFIC_BYTES = 31_678_720
+QGEMM_TRAFFIC_BYTES = 57_473_024 + 12_298_496
 
 
 def peaks():
@@ -159,6 +166,61 @@ def gemv_flops(blocks, M):
 
 
 # ---------------------------------------------------------------------------
+# prefill: BASELINE configs[2] layer at M = 2048 on the tensor-core kernel
+# ---------------------------------------------------------------------------
+
+def prefill_measure(device, reps=20, M=2048, rows=8192, cols=8192):
+    """TFLOP/s of one [rows, cols] 2-bit Lloyd-Max g64 (+0.1% outliers) layer at
+    M tokens (bf16). Each launch is timed alone between CUDA events on the
+    launching stream, with L2 flushed (a 256 MB write) before it."""
+    import torch
+    import tensorshrink_b200 as ts
+    from tensorshrink_b200 import _C, kernels
+
+    _, tc_peak, peak_kind = peaks()
+    w = student_t_cuda((rows, cols), 777, device)
+    d = ts.quantize_device(w, bits=2, group_size=64, outlier_frac=0.001, companded=True)
+    del w
+    ql = ts.QuantLinear.from_device_quant(d)
+    qw = ql.qweight()
+    x = torch.randn(M, cols, device=device).to(torch.bfloat16)
+    out = torch.empty(M, rows, device=device, dtype=torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        kernels.qlinear(x, qw, None, torch.bfloat16, out=out)
+    torch.cuda.synchronize(device)
+    st = torch.cuda.current_stream(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    _C.launch_count(reset=True)
+    for s_ev, e_ev in ev:
+        flush.zero_()
+        s_ev.record(st)
+        kernels.qlinear(x, qw, None, torch.bfloat16, out=out)
+        e_ev.record(st)
+    torch.cuda.synchronize(device)
+    launches = _C.launch_count(reset=True)
+    ms = statistics.median(s_ev.elapsed_time(e_ev) for s_ev, e_ev in ev)
+    assert torch.isfinite(out.float()).all(), "non-finite prefill output"
+    tflops = 2.0 * M * rows * cols / (ms * 1e-3) / 1e12
+    return {
+        "metric": "QuantLinear TFLOP/s (M=2048)",
+        "value": round(tflops, 1), "unit": "TFLOP/s",
+        "config": {"workload": f"lloyd2_g64_outlier0.001_{rows}x{cols}_prefill", "M": M,
+                   "dtype": "bf16 activations, 2-bit codes, fp32 accumulate",
+                   "l2": "flushed (256 MB write) before every timed launch",
+                   "timing": f"median of {reps} single launches between CUDA events"},
+        "ms_per_launch": round(ms, 4),
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "ts::qgemm::qgemm_kernel<2,true,1,256>", "bound": "tensor",
+                     "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / tc_peak, 4), "peak_kind": peak_kind + " bf16 burst",
+                     "flops_per_launch": 2 * M * rows * cols,
+                     # dram read + write bytes of one ncu capture of this launch
+                     "traffic": QGEMM_TRAFFIC_BYTES},
+    }
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 
@@ -208,7 +270,7 @@ def run_ours(args, rank, world, device):
         return ms
 
     # clocks: soak for ~1 s first so the sampler sees steady state, then time
-    soak_until = time.time() + 1.0
+    soak_until = time.time() + args.soak
     while time.time() < soak_until:
         for _ in range(50):
             graph.replay()
@@ -216,7 +278,7 @@ def run_ours(args, rank, world, device):
     with ClockSampler(device.index) as clk:
         ms = timed(graph.replay, args.steps)
         # keep sampling across a comparable stretch when the region is short
-        extra_until = time.time() + 0.5
+        extra_until = time.time() + 0.5 * args.soak
         while time.time() < extra_until:
             for _ in range(50):
                 graph.replay()
@@ -263,6 +325,8 @@ def run_ours(args, rank, world, device):
     torch.cuda.synchronize(device)
     assert torch.isfinite(static_y.float()).all(), "non-finite bench output"
 
+    prefill = prefill_measure(device) if not args.no_prefill else None
+
     out = None
     if rank == 0:
         cpu = cpu_baseline(blocks, M, budget_s=args.cpu_seconds) if world == 1 and not args.no_cpu else None
@@ -297,10 +361,14 @@ def run_ours(args, rank, world, device):
                          "achieved": round(k_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(k_gbs / hbm_peak, 4), "peak_kind": peak_kind,
                          "bytes_per_launch": int(kbytes), "us_per_launch": round(kms * 1e3, 3),
-                         "traffic": None},
+                         # dram__bytes_read.sum + dram__bytes_write.sum of one ncu
+                         # capture of this kernel on one bench layer (same bytes
+                         # for gate, up and down)
+                         "traffic": QGEMV_TRAFFIC_BYTES},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "prefill": prefill,
         }
     return out
 
@@ -401,6 +469,9 @@ def main():
     ap.add_argument("--blocks", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--soak", type=float, default=1.0,
+                    help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

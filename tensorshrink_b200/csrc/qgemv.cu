@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t rb = t0 / KG, kg = t0 - rb * KG;
     for (uint32_t i = 0; t0 + i < t1; ++i) {
       const int s = i % S;
-      if (i >= (uint32_t)S && !mbar_wait(empty + s, ((i / S) - 1) & 1, a.err, 1)) break;
+      if (i >= (uint32_t)S && !mbar_wait_hint(empty + s, ((i / S) - 1) & 1, a.err, 1)) break;
       char* st = stages + s * a.stage_bytes;
       uint32_t* meta = reinterpret_cast<uint32_t*>(st + kTileRows * kPitch);
       const uint32_t row0 = rb * kTileRows;
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   for (uint32_t i = 0; t0 + i < t1; ++i) {
     const int s = i % S;
-    const bool ok = mbar_wait(full + s, (i / S) & 1, a.err, 2);
+    const bool ok = mbar_wait_hint(full + s, (i / S) & 1, a.err, 2);
     const char* st = stages + s * a.stage_bytes;
     const uint32_t* meta = reinterpret_cast<const uint32_t*>(st + kTileRows * kPitch);
     const uint32_t g0 = kg * (uint32_t)a.gpt;
