@@ -783,10 +783,18 @@ bool gemv_supported(const ts_qweight& w) {
   return true;
 }
 
+// Workspace layout, the same for every weight on a device so that one
+// workspace can serve layers of different shapes: the per-CTA partial sums
+// first (each slot is written before it is read, so stale values are
+// harmless), then the 256-byte error-flag block, then one counter per row
+// block (the only part that must start at zero; every call leaves it zeroed).
+static size_t gemv_partials_bytes() {
+  return align_up((size_t)sm_count() * 2 * gemv::kTileRows * gemv::kMaxTok * sizeof(float), 256);
+}
+
 size_t gemv_workspace_size(const ts_qweight& w) {
   const int64_t rbs = (w.rows + gemv::kTileRows - 1) / gemv::kTileRows;
-  return align_up((size_t)rbs * sizeof(int), 256) + 256 +
-         (size_t)sm_count() * 2 * gemv::kTileRows * gemv::kMaxTok * sizeof(float);
+  return gemv_partials_bytes() + 256 + align_up((size_t)rbs * sizeof(int), 256);
 }
 
 // Largest token count per pass that fits shared memory with >= 2 stages.
@@ -816,11 +824,10 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.out = out;
   a.out_dtype = out_dtype;
   a.out_stride = out_stride;
-  const int64_t rbs = (w.rows + gemv::kTileRows - 1) / gemv::kTileRows;
   char* ws = reinterpret_cast<char*>(workspace);
-  a.counters = reinterpret_cast<int*>(ws);
-  a.err = reinterpret_cast<int*>(ws + align_up((size_t)rbs * sizeof(int), 256));
-  a.partials = reinterpret_cast<float*>(ws + align_up((size_t)rbs * sizeof(int), 256) + 256);
+  a.partials = reinterpret_cast<float*>(ws);
+  a.err = reinterpret_cast<int*>(ws + gemv_partials_bytes());
+  a.counters = reinterpret_cast<int*>(ws + gemv_partials_bytes() + 256);
   a.tiles = p.tiles;
   a.kgroups = p.kgroups;
   a.grid = p.grid;

@@ -364,3 +364,22 @@ def test_errors_are_loud():
                                256, 64, torch.float16)
     with pytest.raises(NotImplementedError):
         ts.quantize_device(torch.randn(8, 64, device="cuda"), bits=4, group_size=48)
+
+
+def test_workspace_shared_across_shapes():
+    """One cached workspace serves weights of different row counts in any
+    order (the layout does not depend on the weight's shape)."""
+    import tensorshrink_b200 as ts
+    layers = [_random_layer(r, c, 4, 128, "uniform", False, seed=r + c) for r, c in
+              ((512, 4096), (14336, 4096), (4096, 14336), (1000, 2048))]
+    qls = [ts.QuantLinear.from_device_quant(d) for d in layers]
+    Ws = [torch.from_numpy(goap.dequantize(d.to_quantized_tensor())).cuda() for d in layers]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for rnd in range(3):
+        for i in ((0, 1, 2, 3), (3, 2, 1, 0), (1, 0, 2, 0))[rnd]:
+            M = (1, 8, 3)[rnd]
+            x = torch.randn(M, qls[i].in_features, device="cuda", generator=g).to(torch.bfloat16)
+            y = qls[i](x).float()
+            ref = x.float() @ Ws[i].T
+            err = ((y - ref).abs().max() / ref.abs().max()).item()
+            assert err <= TOL, (rnd, i, err)
