@@ -1,0 +1,128 @@
+"""Tensor-parallel shards on the GPU kernels.
+
+On one GPU: the shards of a layer for 2, 4 and 8 ranks are run through the
+CUDA kernels and combined as the collectives would (sum of fp32 partials for
+row-parallel, concatenation for column-parallel); the result must match the
+unsharded fp32 dequant-matmul within the GEMM tolerance, in the decode (GEMV)
+and prefill (tensor-core) regimes. With two or more GPUs visible, the same
+layers also run as two NCCL ranks.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import goap
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import tensorshrink_b200._C as C
+    C.load()
+    yield
+
+
+def _layer(rows, cols, bits, gs, mode, dq, seed, bias=True):
+    import tensorshrink_b200 as ts
+    w = torch.from_numpy(goap.student_t_weights((rows, cols), seed=seed)).cuda()
+    d = ts.quantize_device(w, bits=bits, group_size=gs, outlier_frac=0.001, double_quant=dq,
+                           nf_quant=mode == "nf", companded=mode == "lloyd")
+    b = (torch.randn(rows, device="cuda") * 0.1).to(torch.bfloat16) if bias else None
+    return ts.QuantLinear.from_device_quant(d, b)
+
+
+def _rel(y, ref):
+    return ((y.float() - ref).abs().max() / ref.abs().max()).item()
+
+
+LAYERS = [
+    (4096, 14336, 4, 128, "uniform", False),   # Llama down projection (row-parallel)
+    (14336, 4096, 4, 128, "uniform", False),   # gate/up (column-parallel)
+    (4096, 4096, 4, 128, "nf", True),          # config 1 layer, double-quant NF4
+    (8192, 8192, 2, 64, "lloyd", False),       # config 3 layer
+]
+
+
+@pytest.mark.parametrize("shape", LAYERS)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_shards_on_one_gpu(shape, world):
+    from tensorshrink_b200 import kernels, tp
+    rows, cols, bits, gs, mode, dq = shape
+    ql = _layer(rows, cols, bits, gs, mode, dq, seed=rows + cols + world)
+    W = ql.dequantize(torch.float32)
+    for M in (1, 256):
+        x = torch.randn(M, cols, device="cuda").to(torch.bfloat16)
+        ref = x.float() @ W.T + ql.bias.float()
+        # row-parallel: fp32 partials summed, bias once
+        acc = torch.zeros(M, rows, device="cuda")
+        for r in range(world):
+            c0, c1 = tp.shard_bounds(ql.padded_cols, world, r, gs)
+            sh = tp.shard_cols(ql, c0, min(c1, cols))
+            acc += kernels.qlinear(x[:, c0:min(c1, cols)].contiguous(), sh.qweight(), None, torch.float32)
+        err = _rel(acc + ql.bias.float(), ref)
+        assert err <= TOL, ("row", M, err)
+        # column-parallel: local outputs concatenated
+        outs = []
+        for r in range(world):
+            r0, r1 = tp.shard_bounds(rows, world, r)
+            outs.append(tp.shard_rows(ql, r0, r1)(x))
+        err = _rel(torch.cat(outs, dim=-1), ref)
+        assert err <= TOL, ("column", M, err)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+        dist.init_process_group("nccl", rank=rank, world_size=world)
+        from tensorshrink_b200 import tp
+        torch.manual_seed(0)
+        ql = _layer(4096, 14336, 4, 128, "uniform", False, seed=5)
+        W = ql.dequantize(torch.float32)
+        errs = []
+        for M in (1, 256):
+            x = torch.randn(M, 14336, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
+            x = x.to(torch.bfloat16)
+            ref = x.float() @ W.T + ql.bias.float()
+            row = tp.RowParallelQuantLinear(ql, input_is_parallel=False)
+            errs.append(_rel(row(x), ref))
+            col = tp.ColumnParallelQuantLinear(ql, gather_output=True)
+            errs.append(_rel(col(x), ref))
+        q.put((rank, errs, None))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_nccl_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs, err in res:
+        assert err is None, (rank, err)
+        assert max(errs) <= TOL, (rank, errs)
