@@ -155,6 +155,10 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
 }
 
 struct Args {
+  // 2-D tensor maps of the metadata arrays ([rows, n_groups]: fp16 scale/min,
+  // or the double-quant code bytes), used when meta_bulk is set
+  CUtensorMap smap;
+  CUtensorMap gmap;
   QW q;
   const void* x;
   int x_dtype;
@@ -181,9 +185,15 @@ struct Args {
   int gbytes_shift;    // log2(bytes of packed codes per group)
   int max_owned_rows;  // capacity of the per-CTA epilogue table
   int x_vec16;         // activation rows are 16-byte aligned
-  int meta_bulk;       // metadata rows are 16-byte aligned: stream them with bulk copies
+  int meta_bulk;       // metadata rows are 16-byte multiples: one 2-D copy per array per tile
   float center;        // C for uniform grids (codebooks use their midpoint)
+  int dq_shift;        // log2(dq_group_size) when it is a power of two, else -1
 };
+
+// super-group index of a flat (row, group) index
+__device__ __forceinline__ uint32_t dq_div(uint32_t flat, const Args& a) {
+  return a.dq_shift >= 0 ? flat >> a.dq_shift : flat / (uint32_t)a.q.dq_gs;
+}
 
 __device__ __forceinline__ uint32_t cta_of(uint64_t t, uint64_t U, uint64_t G) {
   return (uint32_t)(((t + 1) * G + U - 1) / U - 1);
@@ -191,7 +201,7 @@ __device__ __forceinline__ uint32_t cta_of(uint64_t t, uint64_t U, uint64_t G) {
 
 template <int BITS, bool CB, bool DQ, int SEG>
 __global__ void __launch_bounds__(kThreads, 1)
-    qgemv_kernel(const Args a) {
+    qgemv_kernel(const __grid_constant__ Args a) {
   using G = Geo<BITS>;
   extern __shared__ __align__(128) char smem[];
   constexpr int LUT_BYTES = !CB ? 0 : (BITS == 2 ? 256 * 32 * 8 : 256 * 32 * 4);
@@ -240,9 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kConsumerWarps) {
     pdl_launch_dependents();
     uint32_t rb = t0 / KG, kg = t0 - rb * KG;
+    int s = 0;
+    uint32_t ph = 0;          // phase of the ring pass that stage s belongs to
     for (uint32_t i = 0; t0 + i < t1; ++i) {
-      const int s = i % S;
-      if (i >= (uint32_t)S && !mbar_wait_hint(empty + s, ((i / S) - 1) & 1, a.err, 1)) break;
+      if (i >= (uint32_t)S && !mbar_wait_hint(empty + s, ph ^ 1, a.err, 1)) break;
       char* st = stages + s * a.stage_bytes;
       uint32_t* meta = reinterpret_cast<uint32_t*>(st + kTileRows * kPitch);
       const uint32_t row0 = rb * kTileRows;
@@ -252,32 +263,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (a.meta_bulk) {
         // aligned metadata: one bulk copy per (array, row) + one per super array
         const uint32_t ng = min((uint32_t)a.gpt, NGR - g0);            // groups in this tile
-        const uint32_t mb = ng * (DQ ? 1u : 2u);                         // bytes per metadata row
         uint32_t sup_al = 0, sup_bytes = 0;
         if constexpr (DQ) {
-          const uint32_t s_lo = (row0 * NGR + g0) / (uint32_t)a.q.dq_gs;
-          const uint32_t s_hi = ((row0 + nrows - 1) * NGR + g0 + ng - 1) / (uint32_t)a.q.dq_gs;
+          const uint32_t s_lo = dq_div(row0 * NGR + g0, a);
+          const uint32_t s_hi = dq_div((row0 + nrows - 1) * NGR + g0 + ng - 1, a);
           sup_al = s_lo & ~3u;
           sup_bytes = ((s_hi - sup_al + 4) & ~3u) * 4u;
           const uint32_t n_sup_all = (uint32_t)((a.q.rows * (int64_t)NGR + a.q.dq_gs - 1) / a.q.dq_gs);
           sup_bytes = min(sup_bytes, (n_sup_all - sup_al) * 4u);
         }
-        if (lane == 0) mbar_arrive_expect_tx(full + s, nrows * rbytes + 2 * nrows * mb + 2 * sup_bytes);
+        // metadata: one [16 rows x gpt groups] box per array (rows past the end
+        // and groups past n_groups arrive as zeros; the box is counted whole)
+        const uint32_t box_bytes = (uint32_t)kTileRows * (uint32_t)a.gpt * (DQ ? 1u : 2u);
+        if (lane == 0) mbar_arrive_expect_tx(full + s, nrows * rbytes + 2 * box_bytes + 2 * sup_bytes);
         __syncwarp();
         if (lane < (int)nrows)
           bulk_load(st + lane * kPitch,
                     a.q.packed + (size_t)(row0 + lane) * (size_t)a.q.row_bytes + (size_t)kg * kTileK, rbytes, full + s);
-        {
-          const int arr = lane >> 4, r = lane & 15;
-          if (r < (int)nrows) {
-            const uint32_t e = (row0 + r) * NGR + g0;
-            const void* src;
-            if constexpr (DQ)
-              src = (arr == 0 ? a.q.dqs_codes : a.q.dqg_codes) + e;
-            else
-              src = (arr == 0 ? a.q.scale : a.q.gmin) + e;
-            bulk_load(meta + (arr * kTileRows + r) * mrw, src, mb, full + s);
-          }
+        if (lane == 0) {
+          tma_load_2d(meta, &a.smap, (int)g0, (int)row0, full + s);
+          tma_load_2d(meta + kTileRows * mrw, &a.gmap, (int)g0, (int)row0, full + s);
         }
         if constexpr (DQ) {
           if (lane < 2)
@@ -309,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if constexpr (DQ) {
           uint32_t* sup = meta + 2 * kTileRows * mrw;
-          const uint32_t s_al = ((row0 * NGR + g0) / (uint32_t)a.q.dq_gs) & ~3u;
+          const uint32_t s_al = (dq_div(row0 * NGR + g0, a)) & ~3u;
           const uint32_t n_sup_all = (uint32_t)((a.q.rows * (int64_t)NGR + a.q.dq_gs - 1) / a.q.dq_gs);
           for (int j = lane; j < kMaxSupers; j += 32) {
             const uint32_t sidx = s_al + j;
@@ -324,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         kg = 0;
         ++rb;
       }
+      if (++s == S) { s = 0; ph ^= 1; }
     }
     return;
   }
@@ -521,9 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool tok0 = 2 * l < a.mt, tok1 = 2 * l + 1 < a.mt;
   const uint32_t slice_g = (uint32_t)(warp * kSlice) >> a.gbytes_shift;   // first group of the slice in the tile
 
+  int cs = 0;
+  uint32_t cph = 0;
   for (uint32_t i = 0; t0 + i < t1; ++i) {
-    const int s = i % S;
-    const bool ok = mbar_wait_hint(full + s, (i / S) & 1, a.err, 2);
+    const int s = cs;
+    const bool ok = mbar_wait_hint(full + s, cph, a.err, 2);
+    if (++cs == S) { cs = 0; cph ^= 1; }
     const char* st = stages + s * a.stage_bytes;
     const uint32_t* meta = reinterpret_cast<const uint32_t*>(st + kTileRows * kPitch);
     const uint32_t g0 = kg * (uint32_t)a.gpt;
@@ -534,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t* mrow0 = meta + q * mrw;
     const uint32_t* mrow1 = meta + (q + 8) * mrw;
     uint32_t sup_lo = 0;
-    if constexpr (DQ) sup_lo = ((rb * kTileRows * NGR + g0) / (uint32_t)a.q.dq_gs) & ~3u;
+    if constexpr (DQ) sup_lo = dq_div(rb * kTileRows * NGR + g0, a) & ~3u;
     const char* arow0 = st + q * kPitch + warp * kSlice + 4 * l;
     const char* arow1 = arow0 + 8 * kPitch;
     const uint32_t slice_byte0 = kg * (uint32_t)kTileK + warp * kSlice;
@@ -579,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (DQ) {
           const uint32_t* sup = meta + 2 * kTileRows * mrw;
           const uint32_t row = row_q + 8 * r;
-          const uint32_t sj = (row * NGR + g0 + slice_g + gi) / (uint32_t)a.q.dq_gs - sup_lo;
+          const uint32_t sj = dq_div(row * NGR + g0 + slice_g + gi, a) - sup_lo;
           const float2 ms = __half22float2(u2h2(sup[sj]));
           const float2 mg = __half22float2(u2h2(sup[kMaxSupers + sj]));
           const float csv = (float)((mr[off >> 2] >> ((off & 3) * 8)) & 0xFFu);
@@ -679,7 +688,24 @@ int ilog2(int64_t v) {
 struct Plan {
   uint32_t tiles, kgroups, grid;
   int n_chunks, seg_chunks, gpt, meta_row_words, stage_bytes, max_owned_rows;
+  bool meta_bulk;   // metadata rows are 16-byte multiples: 2-D copies into dense row slots
 };
+
+// Metadata of every tile row starts on a 16-byte boundary (and the arrays
+// are 16-byte aligned), so a tile's metadata is one 2-D box per array.
+static bool meta_bulk_ok(const ts_qweight& w, int gpt) {
+  const bool dq = w.dq_scale_codes != nullptr;
+  const int step = dq ? 16 : 8;   // elements per 16 bytes of metadata
+  bool bulk = w.n_groups % step == 0 && gpt % step == 0;
+  if (dq) {
+    const int64_t n_sup = (w.rows * w.n_groups + w.dq_group_size - 1) / w.dq_group_size;
+    bulk = bulk && n_sup % 4 == 0 && is_aligned(w.dq_scale_codes, 16) && is_aligned(w.dq_gmin_codes, 16) &&
+           is_aligned(w.dq_scale_meta, 16) && is_aligned(w.dq_gmin_meta, 16);
+  } else {
+    bulk = bulk && is_aligned(w.scale, 16) && is_aligned(w.gmin, 16);
+  }
+  return bulk;
+}
 
 int lut_bytes(const ts_qweight& w) { return w.codebook ? (w.bits == 2 ? 256 * 32 * 8 : 256 * 32 * 4) : 0; }
 
@@ -694,7 +720,10 @@ Plan make_plan(const ts_qweight& w) {
   p.n_chunks = (int)(w.padded_cols * w.bits / 128);
   p.seg_chunks = (int)std::min<int64_t>(4, gbytes / 16);
   p.gpt = (int)(gemv::kTileK / gbytes);
-  p.meta_row_words = (int)align_up((size_t)((p.gpt + 2 * (E - 1)) / E), 4);  // 16-byte slots
+  p.meta_bulk = meta_bulk_ok(w, p.gpt);
+  // dense rows of exactly gpt elements for the 2-D copies; otherwise 16-byte
+  // slots wide enough for the aligned-down words of a misaligned row
+  p.meta_row_words = p.meta_bulk ? p.gpt / E : (int)align_up((size_t)((p.gpt + 2 * (E - 1)) / E), 4);
   size_t meta = (size_t)2 * gemv::kTileRows * p.meta_row_words * 4;
   if (w.dq_scale_codes) meta += (size_t)2 * gemv::kMaxSupers * 4;
   p.stage_bytes = (int)align_up((size_t)gemv::kTileRows * gemv::kPitch + meta, 128);
@@ -839,19 +868,22 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.max_owned_rows = p.max_owned_rows;
   a.center = 0.f;  // uniform grids use raw codes; codebooks set their midpoint in-kernel
   a.gbytes_shift = ilog2((int64_t)w.group_size * w.bits / 8);
+  a.dq_shift = -1;
+  if (w.dq_group_size > 0 && (w.dq_group_size & (w.dq_group_size - 1)) == 0) a.dq_shift = ilog2(w.dq_group_size);
   const bool dq = w.dq_scale_codes != nullptr;
   a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0;
-  {
-    const int step = dq ? 16 : 8;   // elements per 16 bytes of metadata
-    bool bulk = w.n_groups % step == 0 && p.gpt % step == 0;
-    if (dq) {
-      const int64_t n_sup = (w.rows * w.n_groups + w.dq_group_size - 1) / w.dq_group_size;
-      bulk = bulk && n_sup % 4 == 0 && is_aligned(w.dq_scale_codes, 16) && is_aligned(w.dq_gmin_codes, 16) &&
-             is_aligned(w.dq_scale_meta, 16) && is_aligned(w.dq_gmin_meta, 16);
-    } else {
-      bulk = bulk && is_aligned(w.scale, 16) && is_aligned(w.gmin, 16);
-    }
-    a.meta_bulk = bulk ? 1 : 0;
+  a.meta_bulk = p.meta_bulk ? 1 : 0;
+  if (p.meta_bulk) {
+    const CUtensorMapDataType t = dq ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const uint64_t eb = dq ? 1 : 2;
+    int rc = encode_tmap_2d(&a.smap, dq ? (const void*)w.dq_scale_codes : w.scale, t, (uint64_t)w.n_groups,
+                            (uint64_t)w.rows, (uint64_t)w.n_groups * eb, (uint32_t)p.gpt, gemv::kTileRows,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TS_OK) return rc;
+    rc = encode_tmap_2d(&a.gmap, dq ? (const void*)w.dq_gmin_codes : w.gmin, t, (uint64_t)w.n_groups,
+                        (uint64_t)w.rows, (uint64_t)w.n_groups * eb, (uint32_t)p.gpt, gemv::kTileRows,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TS_OK) return rc;
   }
   const bool cb = w.codebook != nullptr;
   int rc = TS_OK;
