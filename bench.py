@@ -21,7 +21,9 @@ workload ("scaling": "weak"); time is the max over ranks.
 
 The same JSON line carries a `prefill` object: TFLOP/s of the BASELINE
 configs[2] layer ([8192, 8192], 2-bit Lloyd-Max g64, 0.1% outliers) at M=2048
-bf16 on the tensor-core kernel, each launch timed alone after an L2 flush.
+bf16 on the tensor-core kernel, each launch timed alone after an L2 flush,
+and a `quantize` object: fp16-input GB/s of the GPU quantize/pack on the
+BASELINE configs[4] [28672, 8192] shape (4-bit g128, double quant).
 
 --impl reference times the reference algorithm's CPU path (the numpy port
 in oracle/, on all host threads) on a bounded sample of the same workload.
@@ -221,6 +223,48 @@ def prefill_measure(device, reps=20, M=2048, rows=8192, cols=8192):
 
 
 # ---------------------------------------------------------------------------
+# quantize: BASELINE configs[4] weights through the GPU quantize/pack
+# ---------------------------------------------------------------------------
+
+def quantize_measure(device, reps=3, rows=28672, cols=8192):
+    """fp16-input GB/s of the public GPU quantizer (`quantize_device`: top-k
+    outliers, 4-bit g128 codes, double-quant metadata, row-sorted outlier
+    tables) on the largest Llama-70B projection shape, median of `reps` calls
+    timed with CUDA events; plus the projected time for all 68.45 B weights."""
+    import torch
+    import tensorshrink_b200 as ts
+    from tensorshrink_b200 import _C
+
+    w = student_t_cuda((rows, cols), 4242, device)
+    for _ in range(1):
+        ts.quantize_device(w, bits=4, group_size=128, outlier_frac=0.001, double_quant=True)
+    torch.cuda.synchronize(device)
+    times = []
+    _C.launch_count(reset=True)
+    for _ in range(reps):
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        d = ts.quantize_device(w, bits=4, group_size=128, outlier_frac=0.001, double_quant=True)
+        e_ev.record()
+        torch.cuda.synchronize(device)
+        times.append(s_ev.elapsed_time(e_ev))
+    launches = _C.launch_count(reset=True) // reps
+    ms = statistics.median(times)
+    nbytes = rows * cols * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    del d
+    return {
+        "metric": "GPU quantize+pack fp16-input GB/s",
+        "value": round(gbs, 1), "unit": "GB/s",
+        "config": {"workload": f"llama70b_up_{rows}x{cols}_w4g128_dq_outlier0.001", "input_dtype": "fp16",
+                   "timing": f"median of {reps} calls of quantize_device between CUDA events"},
+        "ms_per_call": round(ms, 3),
+        "library_launches_per_call": int(launches),
+        "projected_s_for_68.45B_params": round(68.45e9 * 2 / (gbs * 1e9), 2),
+    }
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 
@@ -326,6 +370,7 @@ def run_ours(args, rank, world, device):
     assert torch.isfinite(static_y.float()).all(), "non-finite bench output"
 
     prefill = prefill_measure(device) if not args.no_prefill else None
+    quant = quantize_measure(device) if not args.no_prefill else None
 
     out = None
     if rank == 0:
@@ -369,6 +414,7 @@ def run_ours(args, rank, world, device):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "quantize": quant,
         }
     return out
 

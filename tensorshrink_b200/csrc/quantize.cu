@@ -85,7 +85,52 @@ struct Geometry {
   const void* w;
   int64_t rows, cols, padded_cols, n_groups, n8;  // n8 = padded_cols / 8 (items per row)
   int gs, bits;
+  uint64_t n8_magic;  // ceil(2^64 / n8) (0 when n8 == 1): row of item i = umul64hi(i, magic)
+  int vec;            // rows are whole 16-byte vectors of 8 elements (cols % 8 == 0, aligned)
 };
+
+// Row of a flat item index: exact for i * n8 < 2^64 (multiply-high by the
+// rounded-up reciprocal instead of a 64-bit division per item).
+__device__ __forceinline__ int64_t row_of(const Geometry& g, int64_t i) {
+  return g.n8_magic ? (int64_t)__umul64hi((uint64_t)i, g.n8_magic) : i;
+}
+
+// 8 consecutive elements of row r starting at column c0 as fp32 values and
+// magnitude keys; columns past the end repeat the last column (codec.py:556
+// pads with the last column).
+template <int DT>
+__device__ __forceinline__ void load8(const Geometry& g, int64_t r, int64_t c0, float (&v)[8], uint32_t (&k)[8]) {
+  if (g.vec && c0 + 8 <= g.cols) {
+    const int64_t e0 = r * g.cols + c0;
+    if (DT == TS_F32) {
+      const uint4 u0 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e0);
+      const uint4 u1 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e0 + 4);
+      const uint32_t b[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = __uint_as_float(b[j]);
+        k[j] = b[j] & 0x7FFFFFFFu;
+      }
+    } else {
+      const uint4 u = ldg_stream_v4(reinterpret_cast<const uint16_t*>(g.w) + e0);
+      const uint32_t b[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t h = (b[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+        v[j] = DT == TS_F16 ? __half2float(__ushort_as_half((uint16_t)h)) : __uint_as_float(h << 16);
+        k[j] = h & 0x7FFFu;
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t c = c0 + j;
+    const int64_t src = r * g.cols + (c < g.cols ? c : g.cols - 1);
+    v[j] = Elem<DT>::val(g.w, src);
+    k[j] = Elem<DT>::key(g.w, src);
+  }
+}
 
 __device__ __forceinline__ float group_reduce_min(float v, int width) {
   for (int o = width / 2; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -103,41 +148,51 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float
                                                          int do_hist) {
   using E = Elem<DT>;
   constexpr int NB = 1 << E::L1_BITS;
-  __shared__ uint32_t h[NB];
+  // one sub-histogram per warp for the 256-bin (16-bit) keys: magnitudes
+  // crowd into a few bins, and fewer threads per counter means fewer
+  // serialized shared-memory atomics
+  constexpr int NSUB = NB <= 256 ? kThreads / 32 : 1;
+  __shared__ uint32_t h[NSUB * NB];
   if (do_hist)
-    for (int i = threadIdx.x; i < NB; i += kThreads) h[i] = 0;
+    for (int i = threadIdx.x; i < NSUB * NB; i += kThreads) h[i] = 0;
   __syncthreads();
+  uint32_t* hw = h + (NSUB > 1 ? (threadIdx.x >> 5) * NB : 0);
   const int gw = g.gs / 8;  // threads per group (power of two <= 32)
   const int64_t items = g.rows * g.n8;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
   for (int64_t base = (int64_t)blockIdx.x * kThreads; base < items; base += stride) {
     const int64_t it = base + threadIdx.x;
     float mn = INFINITY, mx = -INFINITY;
+    int64_t r = 0, c0 = 0;
     if (it < items) {
-      const int64_t r = it / g.n8, c0 = (it - r * g.n8) * 8;
-      const int64_t rowoff = r * g.cols;
+      r = row_of(g, it);
+      c0 = (it - r * g.n8) * 8;
+      float v[8];
+      uint32_t k[8];
+      load8<DT>(g, r, c0, v, k);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int64_t c = c0 + j;
-        const int64_t src = rowoff + (c < g.cols ? c : g.cols - 1);
-        const float v = E::val(g.w, src);
-        mn = fminf(mn, v);
-        mx = fmaxf(mx, v);
-        if (do_hist && c < g.cols) atomicAdd(&h[E::key(g.w, src) >> (E::KEY_BITS - E::L1_BITS)], 1u);
+        mn = fminf(mn, v[j]);
+        mx = fmaxf(mx, v[j]);
+        if (do_hist && c0 + j < g.cols) atomicAdd(&hw[k[j] >> (E::KEY_BITS - E::L1_BITS)], 1u);
       }
     }
     mn = group_reduce_min(mn, gw);
     mx = group_reduce_max(mx, gw);
     if (it < items && (threadIdx.x % gw) == 0) {
-      const int64_t r = it / g.n8, grp = (it - r * g.n8) * 8 / g.gs;
+      const int64_t grp = c0 / g.gs;
       gmin_raw[r * g.n_groups + grp] = mn;
       gmax_raw[r * g.n_groups + grp] = mx;
     }
   }
   if (do_hist) {
     __syncthreads();
-    for (int i = threadIdx.x; i < NB; i += kThreads)
-      if (h[i]) atomicAdd(hist1 + i, h[i]);
+    for (int i = threadIdx.x; i < NB; i += kThreads) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int sub = 0; sub < NSUB; ++sub) t += h[sub * NB + i];
+      if (t) atomicAdd(hist1 + i, t);
+    }
   }
 }
 
@@ -212,13 +267,41 @@ __global__ void __launch_bounds__(kThreads) cta_hist_kernel(const Geometry g, co
   const int64_t r0 = blockIdx.x * plan.rows_per_cta;
   const int64_t r1 = min(g.rows, r0 + plan.rows_per_cta);
   uint32_t above = 0;
-  for (int64_t i = r0 * g.cols + threadIdx.x; i < r1 * g.cols; i += kThreads) {
-    const uint32_t key = E::key(g.w, i);
-    const uint32_t hi = key >> E::LAST_BITS;
-    if (hi > prefix)
-      ++above;
-    else if (hi == prefix)
-      atomicAdd(&h[key & (NB - 1)], 1u);
+  if (g.vec) {
+    // 8 keys per 16/32-byte vector (the range starts on a row, rows are whole vectors)
+    const int64_t e_end = r1 * g.cols;
+    for (int64_t e = r0 * g.cols + 8 * (int64_t)threadIdx.x; e < e_end; e += 8 * kThreads) {
+      uint32_t k[8];
+      if (DT == TS_F32) {
+        const uint4 u0 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e);
+        const uint4 u1 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e + 4);
+        const uint32_t b[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) k[j] = b[j] & 0x7FFFFFFFu;
+      } else {
+        const uint4 u = ldg_stream_v4(reinterpret_cast<const uint16_t*>(g.w) + e);
+        const uint32_t b[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) k[j] = (b[j >> 1] >> (16 * (j & 1))) & 0x7FFFu;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t hi = k[j] >> E::LAST_BITS;
+        if (hi > prefix)
+          ++above;
+        else if (hi == prefix)
+          atomicAdd(&h[k[j] & (NB - 1)], 1u);
+      }
+    }
+  } else {
+    for (int64_t i = r0 * g.cols + threadIdx.x; i < r1 * g.cols; i += kThreads) {
+      const uint32_t key = E::key(g.w, i);
+      const uint32_t hi = key >> E::LAST_BITS;
+      if (hi > prefix)
+        ++above;
+      else if (hi == prefix)
+        atomicAdd(&h[key & (NB - 1)], 1u);
+    }
   }
   atomicAdd(&h[NB], above);
   __syncthreads();
@@ -240,6 +323,17 @@ __global__ void finalize_select_kernel(const uint32_t* cta_hist, int nb, int n_c
   int bin;
   int64_t above_in_level;
   select_bin(tot, nb, st->k_rem, &bin, &above_in_level);
+  // Per CTA: elements above T and ties at T, counted by all threads (one CTA
+  // per thread at a time) into cta_info, then turned into output offsets and
+  // tie shares by one running prefix (ties are granted in CTA order).
+  for (int c = threadIdx.x; c < n_cta; c += blockDim.x) {
+    const uint32_t* h = cta_hist + (size_t)c * (nb + 1);
+    int64_t gt = h[nb];
+    for (int b = bin + 1; b < nb; ++b) gt += h[b];
+    cta_info[2 * c] = gt;
+    cta_info[2 * c + 1] = h[bin];
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     const uint32_t tkey = (st->prefix << (31 - __clz(nb))) | (uint32_t)bin;
     st->t_key = tkey;
@@ -249,33 +343,22 @@ __global__ void finalize_select_kernel(const uint32_t* cta_hist, int nb, int n_c
       st->t_val = __bfloat162float(__ushort_as_bfloat16((uint16_t)tkey));
     else
       st->t_val = __uint_as_float(tkey);
-    // Per CTA: elements above T, ties at T; ties are granted in CTA order.
-    int64_t n_gt = 0, n_eq_total = 0;
-    for (int c = 0; c < n_cta; ++c) {
-      const uint32_t* h = cta_hist + (size_t)c * (nb + 1);
-      int64_t gt = h[nb];
-      for (int b = bin + 1; b < nb; ++b) gt += h[b];
-      n_gt += gt;
-      n_eq_total += h[bin];
-    }
-    (void)n_eq_total;
     (void)key_bits;
     // k = n_gt + need_eq
     const int64_t need = st->k_rem - above_in_level;  // ties needed within the bin
-    st->n_gt = n_gt;
     st->need_eq = need;
-    int64_t off = 0, eq_before = 0;
+    int64_t off = 0, eq_before = 0, n_gt = 0;
     for (int c = 0; c < n_cta; ++c) {
-      const uint32_t* h = cta_hist + (size_t)c * (nb + 1);
-      int64_t gt = h[nb];
-      for (int b = bin + 1; b < nb; ++b) gt += h[b];
-      const int64_t eq = h[bin];
+      const int64_t gt = cta_info[2 * c];
+      const int64_t eq = cta_info[2 * c + 1];
       const int64_t take = i64max(0, i64min(eq, need - eq_before));
       eq_before += eq;
+      n_gt += gt;
       cta_info[2 * c] = off;
       cta_info[2 * c + 1] = take;
       off += gt + take;
     }
+    st->n_gt = n_gt;
   }
 }
 
@@ -357,17 +440,16 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
     uint32_t keys[8];
     int sel_gt = 0, n_eq = 0;
     if (live) {
-      r = it / g.n8;
+      r = row_of(g, it);
       c0 = (it - r * g.n8) * 8;
+      load8<DT>(g, r, c0, v, keys);
+      if (has_t) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t c = c0 + j;
-        const int64_t src = r * g.cols + (c < g.cols ? c : g.cols - 1);
-        v[j] = E::val(g.w, src);
-        keys[j] = E::key(g.w, src);
-        if (has_t && c < g.cols) {
-          sel_gt += keys[j] > tkey;
-          n_eq += keys[j] == tkey;
+        for (int j = 0; j < 8; ++j) {
+          if (c0 + j < g.cols) {
+            sel_gt += keys[j] > tkey;
+            n_eq += keys[j] == tkey;
+          }
         }
       }
     }
@@ -380,19 +462,39 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
       const float gmx = fminf(fmaxf(a.gmax_raw[gi], -tval), tval);
       float scale = __fdiv_rn(__fsub_rn(gmx, gmn), levels);   // codec.py:570
       scale = fmaxf(scale, 1e-8f);                            // codec.py:571
+      // t = (x - gmin) / scale must be the correctly rounded quotient
+      // (codec.py:579-580). A product with the reciprocal is within a few
+      // ulps of it, so it picks the same code unless it lies within a few
+      // ulps of a rounding boundary (a half-integer, or a codebook midpoint);
+      // only then is the exact IEEE division done.
+      const float rs = __frcp_rn(scale);
       uint32_t codes[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float x = fminf(fmaxf(v[j], -tval), tval);      // codec.py:543
-        const float t = __fdiv_rn(__fsub_rn(x, gmn), scale);  // codec.py:579-580
+        const float d = __fsub_rn(x, gmn);
+        float t = __fmul_rn(d, rs);
+        const float tol = fmaxf(fabsf(t), 1.f) * 1e-6f;      // >= 8 ulps of t
         if (a.cb) {
           int lo = 0, hi = a.n_levels - 1;                    // count of mids < t
           while (lo < hi) {
             const int mid = (lo + hi) >> 1;
             if (s_cb_mid[mid] < t) lo = mid + 1; else hi = mid;
           }
+          const bool near = (lo > 0 && fabsf(t - s_cb_mid[lo - 1]) <= tol) ||
+                            (lo < a.n_levels - 1 && fabsf(t - s_cb_mid[lo]) <= tol);
+          if (near) {
+            t = __fdiv_rn(d, scale);
+            lo = 0;
+            hi = a.n_levels - 1;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (s_cb_mid[mid] < t) lo = mid + 1; else hi = mid;
+            }
+          }
           codes[j] = (uint32_t)lo;
         } else {
+          if (fabsf(t - floorf(t) - 0.5f) <= tol) t = __fdiv_rn(d, scale);
           codes[j] = (uint32_t)fminf(fmaxf(rintf(t), 0.f), levels);
         }
       }
@@ -422,16 +524,18 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
       }
     }
     // ---- ordered outlier compaction (index order == thread order) ----
+    // One scan of (elements above T) | (ties at T) << 16: a thread's first
+    // output slot is the count above T before it plus the ties granted
+    // before it (ties go to the lowest indices, up to tie_left).
     if (has_t) {
-      int eq_total;
-      const int eq_before = block_excl_scan(n_eq, &eq_total);
-      int my_sel = sel_gt + (int)i64max(0, i64min(n_eq, tie_left - eq_before));
-      int sel_total;
-      int pos = block_excl_scan(my_sel, &sel_total);
-      if (live && my_sel > 0) {
-        int64_t ties_taken_before = i64max(0, i64min(eq_before, tie_left));
-        int64_t allow = tie_left - ties_taken_before;  // ties this thread may take
-        int64_t p = out_pos + pos;
+      int tot;
+      const int before = block_excl_scan(sel_gt | (n_eq << 16), &tot);
+      const int gt_before = before & 0xFFFF, eq_before = before >> 16;
+      const int gt_total = tot & 0xFFFF, eq_total = tot >> 16;
+      const int64_t ties_before = i64min((int64_t)eq_before, tie_left);
+      int64_t allow = i64max(0, i64min((int64_t)n_eq, tie_left - eq_before));  // ties this thread takes
+      if (live && sel_gt + allow > 0) {
+        int64_t p = out_pos + gt_before + ties_before;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int64_t c = c0 + j;
@@ -448,8 +552,9 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
           }
         }
       }
-      out_pos += sel_total;
-      tie_left = i64max(0, tie_left - eq_total);
+      const int64_t ties_taken = i64min((int64_t)eq_total, tie_left);
+      out_pos += gt_total + ties_taken;
+      tie_left -= ties_taken;
     }
   }
 }
@@ -813,6 +918,11 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
   g.padded_cols = (p.cols + p.group_size - 1) / p.group_size * p.group_size;
   g.n_groups = g.padded_cols / p.group_size;
   g.n8 = g.padded_cols / 8;
+  g.n8_magic = g.n8 > 1 ? ~0ull / (uint64_t)g.n8 + 1 : 0;
+  {
+    const int esz = DT == TS_F32 ? 4 : 2;
+    g.vec = p.cols % 8 == 0 && is_aligned(w, 16) && ((p.cols * esz) % 16 == 0);
+  }
   const int64_t n = p.rows * p.cols;
   const bool outliers = p.k_outliers > 0 && p.k_outliers < n;
   float* gmin_raw = reinterpret_cast<float*>(ws + L.gmin_raw);
