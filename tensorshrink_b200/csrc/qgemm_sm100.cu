@@ -314,34 +314,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    constexpr uint32_t idesc = umma_idesc_f16(XT, kBW, BT);
-    uint32_t ph = 0;
-    int s = 0;
-    bool ok = true;
-    int t_local = 0;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t_local) {
-      if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12)) { ok = false; break; }
-      tc_fence_after();
-      for (int kb = 0; kb < KB; ++kb) {
-        // one lane waits, the warp follows
-        int w_ok = 1;
-        if (lane == 0)
-          w_ok = mbar_wait_hint(ld_full + s, ph, &g_err, 13) && mbar_wait_hint(a_full + s, ph, &g_err, 13);
-        if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
+    // One thread runs the whole loop: tcgen05.mma and tcgen05.commit are
+    // single-thread instructions, and keeping warp-wide synchronization out
+    // of the loop lets the next stage's MMAs follow its barriers at once
+    // (the tensor pipe drains during any gap here).
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(XT, kBW, BT);
+      const uint64_t bd0 = umma_desc_sw128(smem_u32(sX));
+      uint32_t ph = 0;
+      int s = 0;
+      bool ok = true;
+      int t_local = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t_local) {
+        if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12)) { ok = false; break; }
         tc_fence_after();
-        if (lane == 0) {
-          const uint64_t bd = umma_desc_sw128(smem_u32(sX + (size_t)s * kXStageBytes));
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13) || !mbar_wait_hint(a_full + s, ph, &g_err, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // stage s: B descriptor start advances by the stage size (16-byte units)
+          const uint64_t bd = bd0 + (uint64_t)((s * kXStageBytes) >> 4);
           const uint32_t at = tmem + BT + s * kAStageCols;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)   // K=16: 8 TMEM columns of A, +32 bytes of B (+2 in the address field)
             umma_f16_ts(tmem, at + 8 * k, bd + 2 * k, idesc, (kb | k) != 0);
           umma_commit(empty + s);
+          if (++s == S) { s = 0; ph ^= 1; }
         }
-        __syncwarp();
-        if (++s == S) { s = 0; ph ^= 1; }
+        if (ok) umma_commit(tfull);
       }
-      if (lane == 0) umma_commit(tfull);
-      __syncwarp();
     }
   } else if (warp < kFirstDqWarp) {
     // ---------------- epilogue ----------------
