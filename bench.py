@@ -48,8 +48,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "QuantLinear packed-weight HBM GB/s (M=1) & TFLOP/s (M=2048); decode tok/s"
 HIDDEN, INTER = 4096, 14336
 # DRAM bytes per launch (read + write) measured by ncu on this workload
-QGEMV_TRAFFIC_BYTES = 31_678_720
-QGEMM_TRAFFIC_BYTES = 57_473_024 + 12_298_496
+QGEMV_TRAFFIC_BYTES = 31_679_488
+QGEMM_TRAFFIC_BYTES = 57_634_816 + 12_308_736
 
 
 def peaks():
