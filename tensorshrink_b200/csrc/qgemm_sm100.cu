@@ -414,12 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    auto decode = [&](int64_t row, int kb, const uint32_t (&raw)[2], float2 (&sg)[2]) {
-      const int64_t flat = row * q.n_groups + ((kb * kBK + 32 * half) >> a.gs_shift);
+    auto decode = [&](int64_t row_ng, int kb, const uint32_t (&raw)[2], float2 (&sg)[2]) {
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
         if (gi < gph) {
           if (dq) {
+            const int64_t flat = row_ng + ((kb * kBK + 32 * half) >> a.gs_shift);
             const int64_t sup = a.dq_shift >= 0 ? (flat + gi) >> a.dq_shift : (flat + gi) / q.dq_gs;
             const float2 ms = __half22float2(q.dqs_meta[sup]);
             const float2 mg = __half22float2(q.dqg_meta[sup]);
@@ -432,13 +432,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    uint32_t mit = 0, ph = 0;
-    int s = 0;
+    // Ring position of the tile's first stage (ts, tph), and the metadata
+    // block counter; each group walks only its own stages kb = grp, grp+2, ...
+    uint32_t mit = 0, tph = 0;
+    int ts = 0;
     bool ok = true;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + BT + half * (kAStageCols / 2);
+    // Waits for the current metadata block and releases it without using it
+    // (a block that holds none of this group's stages).
+    auto pass_block = [&]() -> bool {
+      if (!mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) return false;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(m_empty + (mit & 1));
+      ++mit;
+      return true;
+    };
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const int64_t row = (int64_t)(tile / a.tblocks) * kBW + rl;
       const bool valid = row < q.rows;
+      const int64_t row_ng = row * q.n_groups;
       // Outliers of this row. Column-sorted rows use a cursor whose next
       // (column, delta) is loaded right after the previous patch, so it has
       // landed by the stage that needs it; other rows scan their list.
@@ -469,27 +481,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       if (sorted) advance();
 
-      for (int kb = 0, mk = 0; kb < KB; ++kb) {
-        // stage slot and phase of this kb, then advance the counters for the next
+      // ring position of this group's first stage in the tile
+      int s = ts + grp;
+      uint32_t ph = tph;
+      while (s >= S) { s -= S; ph ^= 1; }
+      if (a.meta_tma && grp >= KB && !pass_block()) { ok = false; break; }   // no stage of ours in the tile
+      for (int kb = grp; kb < KB; kb += kDqGroups) {
         const int cs = s;
         const uint32_t cph = ph;
-        if (++s == S) { s = 0; ph ^= 1; }
-        const int cmk = mk;
-        if (++mk == spm) mk = 0;
+        s += kDqGroups;
+        while (s >= S) { s -= S; ph ^= 1; }
+        const int cmk = kb % spm;                           // stage within its metadata block
         const int c0 = kb * kBK + 32 * half;               // first column of this thread's half
-        const bool mine = (kb & 1) == grp;
         uint32_t rawc[2] = {0, 0};
         if (a.meta_tma) {
-          // Both groups wait for every metadata block and release it at its
-          // end, so a release can never be counted toward an older use of
-          // the slot.
-          if (cmk == 0 &&
+          // Both groups wait for every metadata block and release it after
+          // their last stage in it, so a release can never be counted toward
+          // an older use of the slot.
+          if (cmk < kDqGroups &&
               !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) { ok = false; break; }
           const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
           const int ib = ((cmk << 6) + 32 * half) >> a.gs_shift;   // group of c0 within the block
 #pragma unroll
           for (int gi = 0; gi < 2; ++gi) {
-            if (mine && gi < gph) {
+            if (gi < gph) {
               if (dq)
                 rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[kBW * 16 + ib + gi] << 8);
               else
@@ -497,19 +512,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                            ((uint32_t)reinterpret_cast<const uint16_t*>(slot + kBW * 16)[ib + gi] << 16);
             }
           }
-          if (cmk == spm - 1 || kb == KB - 1) {
+          if (cmk + kDqGroups >= spm || kb + kDqGroups >= KB) {
             // one arrival per warp: 256 arrivals on one barrier word would
             // serialize in the shared-memory atomic unit every stage
             __syncwarp();
             if (lane == 0) mbar_arrive(m_empty + (mit & 1));
             ++mit;
+            // a one-stage tail block owned by the other group
+            if (kb + kDqGroups >= KB && kb + 1 < KB && (kb + 1) % spm == 0 && !pass_block()) {
+              ok = false;
+              break;
+            }
           }
-        } else if (mine) {
+        } else {
           fetch(tile, kb, rawc);
         }
-        if (!mine) continue;
         float2 sg[2];
-        if (valid) decode(row, kb, rawc, sg);
+        if (valid) decode(row_ng, kb, rawc, sg);
 
         if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15) ||
             !mbar_wait_hint(ld_full + cs, cph, &g_err, 16)) { ok = false; break; }
@@ -563,6 +582,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(a_full + cs);
       }
+      // the next tile starts KB stages later in the ring
+      const int adv = ts + KB;
+      const int wraps = adv / S;
+      ts = adv - wraps * S;
+      tph ^= (uint32_t)(wraps & 1);
     }
   }
 
