@@ -1,5 +1,6 @@
 // C ABI entry points (include/tensorshrink_b200.h): argument validation,
 // dispatch to the kernels, error reporting.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -10,11 +11,39 @@
 namespace ts {
 
 // implemented in qgemv.cu / dequant.cu / quantize.cu / qgemm_sm100.cu
-bool gemv_supported(const ts_qweight& w);
-size_t gemv_workspace_size(const ts_qweight& w);
-int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
-             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
-             void* workspace, size_t ws_bytes, cudaStream_t stream);
+// the two builds of qgemv.cu: one CTA per SM (v1) and two CTAs per SM (v2)
+#define TS_DECLARE_GEMV(ns)                                                                          \
+  namespace ns {                                                                                     \
+  bool gemv_supported(const ts_qweight& w);                                                          \
+  size_t gemv_workspace_size(const ts_qweight& w);                                                   \
+  int gemv_max_tokens(const ts_qweight& w);                                                          \
+  int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,        \
+               const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,      \
+               void* workspace, size_t ws_bytes, cudaStream_t stream);                               \
+  }
+TS_DECLARE_GEMV(gemv_v1)
+TS_DECLARE_GEMV(gemv_v2)
+#undef TS_DECLARE_GEMV
+static bool gemv_supported(const ts_qweight& w) { return gemv_v1::gemv_supported(w); }
+// Workspace covering either build (v2 runs twice the CTAs, so its partial-sum
+// area is larger).
+static size_t gemv_workspace_size(const ts_qweight& w) {
+  size_t n = gemv_v1::gemv_workspace_size(w);
+  if (gemv_v2::gemv_supported(w)) n = std::max(n, gemv_v2::gemv_workspace_size(w));
+  return n;
+}
+// Two CTAs per SM when that build takes all M tokens in one pass and the
+// workspace covers it; one CTA per SM otherwise.
+static int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
+                    const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
+                    void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  if (gemv_v2::gemv_supported(w) && M <= gemv_v2::gemv_max_tokens(w) &&
+      ws_bytes >= gemv_v2::gemv_workspace_size(w))
+    return gemv_v2::run_gemv(w, x, x_dtype, M, x_stride, bias, bias_dtype, out, out_dtype, out_stride,
+                             workspace, ws_bytes, stream);
+  return gemv_v1::run_gemv(w, x, x_dtype, M, x_stride, bias, bias_dtype, out, out_dtype, out_stride,
+                           workspace, ws_bytes, stream);
+}
 int run_generic_qlinear(const ts_qweight& w, const void* x, int x_dtype, int64_t M,
                         int64_t x_stride, const void* bias, int bias_dtype, void* out,
                         int out_dtype, int64_t out_stride, cudaStream_t stream);
@@ -312,7 +341,7 @@ extern "C" int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtyp
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != TS_OK) return rc;
-  const size_t need = gemv_supported(*w) ? gemv_workspace_size(*w) : 0;
+  const size_t need = gemv_supported(*w) ? gemv_v1::gemv_workspace_size(*w) : 0;   // the one-CTA-per-SM build runs here
   TS_UNSUPPORTED(need <= kNoAllocScratchBytes,
                  "ts_qlinear_noalloc: weight of %lld rows needs %zu bytes of scratch, above the "
                  "fixed %zu; use ts_qlinear with a caller workspace",

@@ -43,10 +43,25 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+// This file is compiled twice: as is (16 consumer warps, one CTA per SM,
+// namespace ts::gemv_v1) and from qgemv_x2.cu (8 consumer warps, two CTAs per
+// SM, namespace ts::gemv_v2). The entry point picks per call.
+#ifndef TS_GEMV_NS
+#define TS_GEMV_NS gemv_v1
+#endif
+
 namespace ts {
+namespace TS_GEMV_NS {
 namespace gemv {
 
-constexpr int kConsumerWarps = 16;
+#ifndef TS_GEMV_CW
+#define TS_GEMV_CW 16
+#endif
+#ifndef TS_GEMV_CPS
+#define TS_GEMV_CPS 1
+#endif
+constexpr int kConsumerWarps = TS_GEMV_CW;   // consumer warps per CTA
+constexpr int kCtasPerSm = TS_GEMV_CPS;      // resident CTAs per SM (grid = SMs x this)
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
 constexpr int kTileRows = 16;
@@ -200,7 +215,7 @@ __device__ __forceinline__ uint32_t cta_of(uint64_t t, uint64_t U, uint64_t G) {
 }
 
 template <int BITS, bool CB, bool DQ, int SEG>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     qgemv_kernel(const __grid_constant__ Args a) {
   using G = Geo<BITS>;
   extern __shared__ __align__(128) char smem[];
@@ -716,7 +731,7 @@ Plan make_plan(const ts_qweight& w) {
   p.kgroups = (uint32_t)((w.packed_row_bytes + gemv::kTileK - 1) / gemv::kTileK);
   const uint32_t rbs = (uint32_t)((w.rows + gemv::kTileRows - 1) / gemv::kTileRows);
   p.tiles = rbs * p.kgroups;
-  p.grid = std::max<uint32_t>(1, std::min<uint32_t>((uint32_t)sm_count(), p.tiles));
+  p.grid = std::max<uint32_t>(1, std::min<uint32_t>((uint32_t)sm_count() * gemv::kCtasPerSm, p.tiles));
   p.n_chunks = (int)(w.padded_cols * w.bits / 128);
   p.seg_chunks = (int)std::min<int64_t>(4, gbytes / 16);
   p.gpt = (int)(gemv::kTileK / gbytes);
@@ -744,7 +759,7 @@ size_t fixed_smem(const ts_qweight& w, const Plan& p, int mt) {
          (size_t)gemv::kCbuf * 4 + 2 * gemv::kMaxStages * 8 + 64;
 }
 
-size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024); }
+size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024 / gemv::kCtasPerSm - (gemv::kCtasPerSm - 1) * 1024); }
 
 int stages_for(const ts_qweight& w, const Plan& p, int mt) {
   const size_t f = fixed_smem(w, p, mt);
@@ -903,5 +918,5 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   return TS_OK;
 }
 
+}  // namespace TS_GEMV_NS
 }  // namespace ts
-

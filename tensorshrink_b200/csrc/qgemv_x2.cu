@@ -1,0 +1,10 @@
+// Decode GEMV with two CTAs per SM (8 consumer warps each, about half the
+// shared memory each): one CTA's prologue (activation staging, outlier and
+// bias table) overlaps the other CTA's streaming. Used when its shared-memory
+// plan holds every token of the call in one pass and the caller's workspace
+// covers its larger partial-sum area (twice the CTAs); otherwise the
+// one-CTA-per-SM build of the same source runs.
+#define TS_GEMV_NS gemv_v2
+#define TS_GEMV_CW 8
+#define TS_GEMV_CPS 2
+#include "qgemv.cu"
