@@ -103,7 +103,7 @@ TS_API int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M
 /*
  * Allocation-free variant of ts_qlinear (no counterpart in the reference):
  * same arguments minus the workspace. The decode kernel's scratch lives in a
- * fixed per-device array of ts_qlinear_noalloc_max_scratch() bytes (256 KiB)
+ * fixed per-device array of ts_qlinear_noalloc_max_scratch() bytes (512 KiB)
  * inside the library, for callers that cannot allocate device memory. A
  * weight whose ts_qlinear_workspace_size() exceeds that returns
  * TS_ERR_UNSUPPORTED. The first call on each device resolves the array's

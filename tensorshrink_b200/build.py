@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import argparse
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -49,9 +50,21 @@ def _deps_mtime() -> float:
     return max(f.stat().st_mtime for f in files)
 
 
+def _included_cu(src: Path) -> list[Path]:
+    """`.cu` files that `src` includes by name (a source compiled twice with
+    different macros includes the other one)."""
+    out = []
+    for m in re.finditer(r'^#include "([^"]+\.cu)"', src.read_text(), re.M):
+        f = CSRC / m.group(1)
+        if f.exists():
+            out.append(f)
+    return out
+
+
 def _compile(src: Path, verbose: bool) -> Path:
     obj = OBJDIR / (src.stem + ".o")
-    if obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, _deps_mtime()):
+    newest = max([src.stat().st_mtime, _deps_mtime()] + [f.stat().st_mtime for f in _included_cu(src)])
+    if obj.exists() and obj.stat().st_mtime >= newest:
         return obj
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
     if verbose:

@@ -305,7 +305,7 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
 // on it: serialize them.
 namespace ts {
 namespace {
-constexpr size_t kNoAllocScratchBytes = 256u << 10;
+constexpr size_t kNoAllocScratchBytes = 512u << 10;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
@@ -341,7 +341,7 @@ extern "C" int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtyp
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != TS_OK) return rc;
-  const size_t need = gemv_supported(*w) ? gemv_v1::gemv_workspace_size(*w) : 0;   // the one-CTA-per-SM build runs here
+  const size_t need = gemv_supported(*w) ? gemv_workspace_size(*w) : 0;
   TS_UNSUPPORTED(need <= kNoAllocScratchBytes,
                  "ts_qlinear_noalloc: weight of %lld rows needs %zu bytes of scratch, above the "
                  "fixed %zu; use ts_qlinear with a caller workspace",

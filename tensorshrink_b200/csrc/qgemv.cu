@@ -832,8 +832,13 @@ bool gemv_supported(const ts_qweight& w) {
 // first (each slot is written before it is read, so stale values are
 // harmless), then the 256-byte error-flag block, then one counter per row
 // block (the only part that must start at zero; every call leaves it zeroed).
+// Both builds of this file (one and two CTAs per SM) use the same layout,
+// sized for the larger grid, because one workspace serves calls of either:
+// two partial slots per CTA of a grid of SMs x kLayoutCtasPerSm.
+constexpr int kLayoutCtasPerSm = 2;
+static_assert(gemv::kCtasPerSm <= kLayoutCtasPerSm, "workspace layout sized for at most two CTAs per SM");
 static size_t gemv_partials_bytes() {
-  return align_up((size_t)sm_count() * 2 * gemv::kTileRows * gemv::kMaxTok * sizeof(float), 256);
+  return align_up((size_t)sm_count() * kLayoutCtasPerSm * 2 * gemv::kTileRows * gemv::kMaxTok * sizeof(float), 256);
 }
 
 size_t gemv_workspace_size(const ts_qweight& w) {
