@@ -19,17 +19,21 @@
 // tile row: 8 chunks of 16 bytes, each one m16 x k tensor-core step. Lane
 // (q, l) = (lane/4, lane%4) holds rows q and q+8 and reads the 4-byte word at
 // 4l of a chunk, so the k of every MMA come from one chunk and hence one
-// quantization group. Codes become fp16 (v - C) values in registers (uniform
-// grids: the exponent-bias trick, integer codes OR-ed into the mantissa of
-// 1024.0; NF / Lloyd-Max codebooks: a per-lane byte lookup table in shared
-// memory) and feed mma.sync m16n8k16 with fp32 accumulation; the 8 columns
-// are the (up to 8) tokens. The k order inside an MMA is free, so the
-// activations (B) are staged in exactly the order the code words unpack. Per
-// (row, group) the reconstruction is w = v*s + g, so
+// quantization group. The k order inside an MMA is free, so the activations
+// (B) are staged in exactly the order the code words unpack. Per (row, group)
+// the reconstruction is w = v*s + g, so
 //   sum_k x_k w_k = s * sum_k x_k (v_k - C) + (g + C*s) * sum_k x_k ,
-// applied once per group segment with the segment's fp32 activation sum. The
-// activations are staged as fp16 scaled by a power of two per segment (exact
-// rescale into [-1, 1]).
+// applied once per group segment with the segment's fp32 activation sum.
+//  - Uniform grids (C = 0, v = the integer code): codes are masked out of
+//    the word as bytes (one AND, or shift + AND, per 4 codes) and feed
+//    mma.sync m16n8k32 u8 x s8 with exact s32 accumulation. Activations are
+//    staged as 15-bit fixed point per segment, x = f (256 hi + lo) with f a
+//    power of two and hi, lo signed bytes; hi and lo of a token are two
+//    adjacent B columns, so one MMA serves 4 tokens (two MMAs for 5..8).
+//  - NF / Lloyd-Max codebooks: a per-lane byte lookup table in shared memory
+//    gives fp16 (v - C) pairs for mma.sync m16n8k16 with fp32 accumulation;
+//    the 8 columns are the tokens, staged as fp16 scaled by a power of two
+//    per segment (exact rescale into [-1, 1]).
 //
 // Row blocks wholly inside one CTA's range are finished by that CTA; a row
 // block split between CTAs is finished by whichever CTA arrives last (per
@@ -72,7 +76,6 @@ constexpr int kMaxStages = 6;
 constexpr int kMaxTok = 8;
 constexpr int kMaxSupers = 64;                     // double-quant super-groups per tile
 constexpr int kOutCap = 2048;                      // outliers preloaded per CTA (more: read in place)
-constexpr int kCbuf = 2048;                        // outlier contributions per epilogue pass
 
 template <int BITS>
 struct Geo {
@@ -94,54 +97,16 @@ __device__ __forceinline__ uint32_t hfma(uint32_t a, uint32_t b, uint32_t c) {
   return h22u(__hfma2(u2h2(a), u2h2(b), u2h2(c)));
 }
 
-// Offsets (within the word's codes) of the two codes that pair p holds.
-template <int BITS, bool CB>
-__host__ __device__ __forceinline__ int2 pair_off(int p) {
-  if (!CB && BITS == 4) return make_int2(p, p + 4);
-  if (!CB && BITS == 2) return make_int2(p, p + 8);
-  return make_int2(2 * p, 2 * p + 1);
-}
-
-// Code multiplier m of pair p in the raw uniform-grid unpacking (the pair
-// holds 1024 + m*code); codebook lookups hold v - C directly (m = 1).
-template <int BITS, bool CB>
-__host__ __device__ __forceinline__ float pair_mult(int p) {
-  if (!CB && BITS == 4) return (p & 1) ? 16.f : 1.f;
-  if (!CB && BITS == 2) return (float)(1 << (2 * (p & 3)));
-  return 1.f;
-}
-
-// Unpack one 32-bit word of codes into PPW fp16 pairs, in the order
-// the MMAs consume them. `lut` points at this lane's lookup-table column.
-template <int BITS, bool CB>
-__device__ __forceinline__ void expand(uint32_t q, const char* lut, uint32_t (&P)[Geo<BITS>::PPW]) {
-  if constexpr (!CB && BITS == 4) {
-    // (1024 + m*n) with m = 1 (pairs 0, 2) or 16 (pairs 1, 3); the 1024 and
-    // the m are removed on the activation side (see pair_mult)
-    const uint32_t q2 = q >> 8;
-    P[0] = lop_and_or(q, 0x000F000Fu, 0x64006400u);
-    P[1] = lop_and_or(q, 0x00F000F0u, 0x64006400u);
-    P[2] = lop_and_or(q2, 0x000F000Fu, 0x64006400u);
-    P[3] = lop_and_or(q2, 0x00F000F0u, 0x64006400u);
-  } else if constexpr (!CB && BITS == 2) {
-    // (1024 + m*n) with m = 1, 4, 16, 64 by crumb position
-    const uint32_t q2 = q >> 8;
-    P[0] = lop_and_or(q, 0x00030003u, 0x64006400u);
-    P[1] = lop_and_or(q, 0x000C000Cu, 0x64006400u);
-    P[2] = lop_and_or(q, 0x00300030u, 0x64006400u);
-    P[3] = lop_and_or(q, 0x00C000C0u, 0x64006400u);
-    P[4] = lop_and_or(q2, 0x00030003u, 0x64006400u);
-    P[5] = lop_and_or(q2, 0x000C000Cu, 0x64006400u);
-    P[6] = lop_and_or(q2, 0x00300030u, 0x64006400u);
-    P[7] = lop_and_or(q2, 0x00C000C0u, 0x64006400u);
-  } else if constexpr (!CB && BITS == 8) {
-    P[0] = __byte_perm(q, 0x64646464u, 0x5140);                                         // 1024 + b
-    P[1] = __byte_perm(q, 0x64646464u, 0x5342);
-  } else if constexpr (CB && BITS == 4) {
+// Codebook codes of one 32-bit word as PPW fp16 pairs (v - C) of consecutive
+// codes, in the order the MMAs consume them. `lut` points at this lane's
+// lookup-table column.
+template <int BITS>
+__device__ __forceinline__ void expand_cb(uint32_t q, const char* lut, uint32_t (&P)[Geo<BITS>::PPW]) {
+  if constexpr (BITS == 4) {
     // lut: [256 bytes][32 lanes] half2 (v(lo)-C, v(hi)-C)
 #pragma unroll
     for (int i = 0; i < 4; ++i) P[i] = *reinterpret_cast<const uint32_t*>(lut + ((q >> (8 * i)) & 0xFFu) * 128u);
-  } else if constexpr (CB && BITS == 2) {
+  } else if constexpr (BITS == 2) {
     // lut: [256][32 lanes] uint2 = two half2 (crumbs 0,1 | 2,3)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -167,6 +132,23 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
       "{%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Integer MMA: u8 codes (A, 16 rows x 32 k) times s8 activation bytes
+// (B, 32 k x 8 columns), exact s32 accumulation.
+__device__ __forceinline__ void imma16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four ints' low bytes packed into one word (byte 0 first).
+__device__ __forceinline__ uint32_t pack_bytes(int b0, int b1, int b2, int b3) {
+  return __byte_perm(__byte_perm((uint32_t)b0, (uint32_t)b1, 0x0040), __byte_perm((uint32_t)b2, (uint32_t)b3, 0x0040),
+                     0x5410);
 }
 
 struct Args {
@@ -201,7 +183,6 @@ struct Args {
   int max_owned_rows;  // capacity of the per-CTA epilogue table
   int x_vec16;         // activation rows are 16-byte aligned
   int meta_bulk;       // metadata rows are 16-byte multiples: one 2-D copy per array per tile
-  float center;        // C for uniform grids (codebooks use their midpoint)
   int dq_shift;        // log2(dq_group_size) when it is a power of two, else -1
 };
 
@@ -227,18 +208,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   char* lut = smem + S * a.stage_bytes;
   const int n_mma = a.n_chunks * G::MPW;
   const int tok_stride = n_mma * 4 + 4;              // uint2 per token (+32 B pad)
+  const int xcols = 2 * a.mt;                        // integer path: B columns (hi, lo per token) per MMA
   uint2* xb = reinterpret_cast<uint2*>(lut + LUT_BYTES);
   const int n_seg = a.n_chunks / a.seg_chunks;
-  // per (token, segment): (2^e, sum x, sum of the uniform-grid offsets 1024/m * x~, 0)
+  // per (token, segment): (activation scale, sum x, 0, 0)
   float4* sx = reinterpret_cast<float4*>(xb + a.mt * tok_stride);
   float* epi = reinterpret_cast<float*>(sx + a.mt * n_seg);
   float* red = epi + a.max_owned_rows * kMaxTok;
   int* o_ptr = reinterpret_cast<int*>(red + kConsumerWarps * kTileRows * kMaxTok);   // [owned rows + 1]
   int* o_col = o_ptr + a.max_owned_rows + 4;                                            // [kOutCap]
-  float* o_dl = reinterpret_cast<float*>(o_col + kOutCap);                              // [kOutCap]
-  float* o_bias = o_dl + kOutCap;                                                       // [owned rows]
-  float* cbuf = o_bias + a.max_owned_rows + 4;                                           // [kCbuf]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(cbuf + kCbuf);
+  uint32_t* o_dw = reinterpret_cast<uint32_t*>(o_col + kOutCap);   // [kOutCap / 2 + 1] fp16 deltas as words
+  float* o_bias = reinterpret_cast<float*>(o_dw + kOutCap);                             // [owned rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(o_bias + a.max_owned_rows + 4);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   int* s_flag = reinterpret_cast<int*>(bars + 2 * kMaxStages);
@@ -350,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
 
   // ------------------------------------------------------------------ consumers
-  float center = a.center;
+  float center = 0.f;   // codebooks: the midpoint C of the table
   if constexpr (CB) {
     const float* cb = a.q.codebook;
     center = 0.5f * (__ldg(cb) + __ldg(cb + (1 << BITS) - 1));
@@ -385,9 +366,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   named_bar_sync(1, kConsumerThreads);
   const int o_base = n_own_rows > 0 ? o_ptr[0] : 0;
   const int o_cnt = n_own_rows > 0 ? o_ptr[n_own_rows] - o_base : 0;
-  for (int j = threadIdx.x; j < min(o_cnt, kOutCap); j += kConsumerThreads) {
-    o_col[j] = __ldg(a.q.ocol + o_base + j);
-    o_dl[j] = __half2float(__ldg(a.q.odelta + o_base + j));
+  // the first kOutCap outliers of the slice into shared memory with async
+  // copies, in flight while the activations load: columns as 4-byte words,
+  // deltas as the 4-byte words covering them (o_dw holds delta j at half
+  // index j + dl_off), zero-filled past the end of the array
+  const int n_pre = min(o_cnt, kOutCap);
+  const int dl_off = o_base & 1;
+  for (int j = threadIdx.x; j < n_pre; j += kConsumerThreads) cp_async4(o_col + j, a.q.ocol + o_base + j, 4);
+  if ((reinterpret_cast<uintptr_t>(a.q.odelta) & 3) == 0) {
+    const int64_t h0 = (int64_t)o_base - dl_off;
+    const int nw = (n_pre + dl_off + 1) >> 1;
+    for (int w = threadIdx.x; w < nw; w += kConsumerThreads) {
+      const int64_t left = a.q.n_outliers - (h0 + 2 * w);   // halves from this word to the end
+      cp_async4(o_dw + w, a.q.odelta + h0 + 2 * w, left >= 2 ? 4 : 2);
+    }
+  } else {
+    for (int j = threadIdx.x; j < n_pre; j += kConsumerThreads)
+      reinterpret_cast<__half*>(o_dw)[j + dl_off] = __ldg(a.q.odelta + o_base + j);
   }
 
   // x is produced by the previous kernel in the stream (programmatic launch)
@@ -438,89 +433,151 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       // power-of-two scale 2^e with max|x| / 2^e in [0.5, 1): exponent bits
       const int e = mx > 0.f ? min(126, (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 126) : 0;
-      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
-      float hx[16];
+      if constexpr (CB) {
+        const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+        float hx[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) hx[j] = v[j] * inv;
-      // B fragments (x~ / m of each pair) and, for uniform grids, the constant
-      // sum over k of (1024 / m_k) * x~_k carried by the raw unpacked codes
-      float xc = 0.f;
-      uint2 frag[16 / G::KPW][G::MPW];
-#pragma unroll
-      for (int wb = 0; wb < 16 / G::KPW; ++wb) {
-#pragma unroll
-        for (int m = 0; m < G::MPW; ++m) {
-          uint32_t bw[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int pr = 2 * m + h;
-            const int2 o = pair_off<BITS, CB>(pr);
-            const float im = 1.f / pair_mult<BITS, CB>(pr);
-            const half2 hv = __floats2half2_rn(hx[wb * G::KPW + o.x] * im, hx[wb * G::KPW + o.y] * im);
-            bw[h] = h22u(hv);
-            if constexpr (!CB) {
-              const float2 f2 = __half22float2(hv);
-              xc += 1024.f * (f2.x + f2.y);
-            }
-          }
-          frag[wb][m] = make_uint2(bw[0], bw[1]);
-        }
-      }
-      for (int o = tps / 2; o > 0; o >>= 1) xc += __shfl_xor_sync(0xffffffffu, xc, o);
-      if (live) {
-        const uint32_t sg = k0 / seg_k;
-        if (k0 % seg_k == 0)
-          sx[n * n_seg + sg] = make_float4(__uint_as_float((uint32_t)(e + 127) << 23), sum, xc, 0.f);
+        for (int j = 0; j < 16; ++j) hx[j] = v[j] * inv;
+        // B fragments: pair p of a word holds its codes 2p, 2p+1
+        uint2 frag[16 / G::KPW][G::MPW];
 #pragma unroll
         for (int wb = 0; wb < 16 / G::KPW; ++wb) {
-          const uint32_t gwb = k0 / G::KPW + wb;     // global word-block index
-          const uint32_t ch = gwb >> 2, l = gwb & 3;
 #pragma unroll
-          for (int m = 0; m < G::MPW; ++m) xb[n * tok_stride + (ch * G::MPW + m) * 4 + l] = frag[wb][m];
+          for (int m = 0; m < G::MPW; ++m) {
+            uint32_t bw[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int pr = 2 * m + h;
+              bw[h] = h22u(__floats2half2_rn(hx[wb * G::KPW + 2 * pr], hx[wb * G::KPW + 2 * pr + 1]));
+            }
+            frag[wb][m] = make_uint2(bw[0], bw[1]);
+          }
+        }
+        if (live) {
+          const uint32_t sg = k0 / seg_k;
+          if (k0 % seg_k == 0)
+            sx[n * n_seg + sg] = make_float4(__uint_as_float((uint32_t)(e + 127) << 23), sum, 0.f, 0.f);
+#pragma unroll
+          for (int wb = 0; wb < 16 / G::KPW; ++wb) {
+            const uint32_t gwb = k0 / G::KPW + wb;     // global word-block index
+            const uint32_t ch = gwb >> 2, l = gwb & 3;
+#pragma unroll
+            for (int m = 0; m < G::MPW; ++m) xb[n * tok_stride + (ch * G::MPW + m) * 4 + l] = frag[wb][m];
+          }
+        }
+      } else {
+        // uniform grids: x~ = rint(x 2^(14-e)) (|x~| <= 2^14, 15-bit fixed
+        // point per segment) split into signed bytes x~ = 256 hi + lo with lo
+        // in [-128, 128); hi and lo of token n are the B columns 2n, 2n+1 of
+        // the integer MMAs, whose k order follows the code unpacking below
+        const int ec = max(e, -112);
+        const float up = __uint_as_float((uint32_t)(141 - ec) << 23);
+        int hi[16], lo[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int xi = __float2int_rn(v[j] * up);
+          lo[j] = (xi << 24) >> 24;
+          hi[j] = (xi - lo[j]) >> 8;
+        }
+        if (live) {
+          const uint32_t sg = k0 / seg_k;
+          if (k0 % seg_k == 0)
+            sx[n * n_seg + sg] = make_float4(__uint_as_float((uint32_t)(113 + ec) << 23), sum, 0.f, 0.f);
+          uint2* xh = xb + (2 * n) * 4;       // column 2n (hi); column 2n+1 (lo) follows at +4
+          if constexpr (BITS == 4) {
+            // 32-code chunk = one MMA; lane l holds codes 8l..8l+7: even codes
+            // (low nibbles) in b0, odd codes in b1
+            const uint32_t J = k0 >> 5, lb = (k0 & 31) >> 3;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int* H = hi + 8 * u;
+              const int* L = lo + 8 * u;
+              xh[J * xcols * 4 + lb + u] = make_uint2(pack_bytes(H[0], H[2], H[4], H[6]), pack_bytes(H[1], H[3], H[5], H[7]));
+              xh[J * xcols * 4 + 4 + lb + u] =
+                  make_uint2(pack_bytes(L[0], L[2], L[4], L[6]), pack_bytes(L[1], L[3], L[5], L[7]));
+            }
+          } else if constexpr (BITS == 2) {
+            // 64-code chunk = two MMAs; lane l holds codes 16l + 4j + t (crumb t
+            // of byte j): MMA m takes crumbs 2m (b0) and 2m+1 (b1)
+            const uint32_t l16 = (k0 & 63) >> 4, J0 = (k0 >> 6) * 2;
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              xh[(J0 + m) * xcols * 4 + l16] = make_uint2(pack_bytes(hi[2 * m], hi[4 + 2 * m], hi[8 + 2 * m], hi[12 + 2 * m]),
+                                                         pack_bytes(hi[2 * m + 1], hi[5 + 2 * m], hi[9 + 2 * m], hi[13 + 2 * m]));
+              xh[(J0 + m) * xcols * 4 + 4 + l16] =
+                  make_uint2(pack_bytes(lo[2 * m], lo[4 + 2 * m], lo[8 + 2 * m], lo[12 + 2 * m]),
+                             pack_bytes(lo[2 * m + 1], lo[5 + 2 * m], lo[9 + 2 * m], lo[13 + 2 * m]));
+            }
+          } else {
+            // 16-code chunk = half an MMA: even chunks in b0 (k 0..15), odd in b1
+            const uint32_t ch = k0 >> 4, J = ch >> 1, h = ch & 1;
+            uint32_t* xw = reinterpret_cast<uint32_t*>(xh + J * xcols * 4);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              xw[2 * u + h] = pack_bytes(hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
+              xw[8 + 2 * u + h] = pack_bytes(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
+            }
+          }
         }
       }
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   named_bar_sync(1, kConsumerThreads);
   {
-    // epilogue table: bias + sum over the row's outliers of x[:, col] * delta.
-    // Contributions are computed one thread per (outlier, token) into `cbuf`
-    // (activations read back from the staged fragments: x = x~ * m * 2^e),
-    // then summed per row in outlier order (deterministic), in passes of
-    // kCbuf / mt outliers.
+    // epilogue table: bias + sum over the row's outliers, in stored order, of
+    // x[:, col] * delta; one thread per (row, token). The activations are read
+    // back from the staged B fragments (codebooks: x = x~ 2^e; uniform grids:
+    // x = f (256 hi + lo)). Entries of tokens >= mt are never stored.
     const int seg_k = a.seg_chunks * G::KPC;
     const int seg_sh = 31 - __clz(seg_k);
-    for (int i = threadIdx.x; i < n_own; i += kConsumerThreads)
-#pragma unroll
-      for (int n = 0; n < kMaxTok; ++n) epi[i * kMaxTok + n] = i < n_own_rows ? o_bias[i] : 0.f;
-    const int per_pass = kCbuf / a.mt;
-    for (int j0 = 0; j0 < o_cnt; j0 += per_pass) {
-      const int jn = min(per_pass, o_cnt - j0);
-      named_bar_sync(1, kConsumerThreads);
-      for (int it = threadIdx.x; it < jn * a.mt; it += kConsumerThreads) {
-        const int jj = it / a.mt, n = it - jj * a.mt, j = j0 + jj;
+    const __half* o_dh = reinterpret_cast<const __half*>(o_dw) + dl_off;
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(xb);
+    for (int it = threadIdx.x; it < n_own_rows * a.mt; it += kConsumerThreads) {
+      const int i = it / a.mt, n = it - i * a.mt;
+      float c = o_bias[i];
+      const int j_end = o_ptr[i + 1] - o_base;
+      for (int j = o_ptr[i] - o_base; j < j_end; ++j) {
         const int col = j < kOutCap ? o_col[j] : __ldg(a.q.ocol + o_base + j);
-        const float d = j < kOutCap ? o_dl[j] : __half2float(__ldg(a.q.odelta + o_base + j));
-        const int wb = col / G::KPW, o = col - wb * G::KPW;
-        int p, hi;
-        if (!CB && BITS == 4) { p = o & 3; hi = o >> 2; }
-        else if (!CB && BITS == 2) { p = o & 7; hi = o >> 3; }
-        else { p = o >> 1; hi = o & 1; }
-        const int J = (wb >> 2) * G::MPW + (p >> 1), l = wb & 3;
-        const uint2 u = xb[n * tok_stride + J * 4 + l];
-        const uint32_t hw = (p & 1) ? u.y : u.x;
-        const float xv = __half2float(__ushort_as_half((uint16_t)(hw >> (16 * hi)))) * pair_mult<BITS, CB>(p) *
-                         sx[n * n_seg + (col >> seg_sh)].x;
-        cbuf[jj * a.mt + n] = xv * d;
+        const float d = __half2float(j < kOutCap ? o_dh[j] : __ldg(a.q.odelta + o_base + j));
+        const float f = sx[n * n_seg + (col >> seg_sh)].x;
+        float xv;
+        if constexpr (CB) {
+          const int wb = col / G::KPW, o = col - wb * G::KPW;
+          const int p = o >> 1, hi = o & 1;
+          const int J = (wb >> 2) * G::MPW + (p >> 1), lw = wb & 3;
+          const uint2 u = xb[n * tok_stride + J * 4 + lw];
+          const uint32_t hw = (p & 1) ? u.y : u.x;
+          xv = __half2float(__ushort_as_half((uint16_t)(hw >> (16 * hi)))) * f;
+        } else {
+          int J, lw, h, j8;   // MMA, lane, b0/b1, byte of the code's activation (see the staging)
+          if constexpr (BITS == 4) {
+            const int cc = col & 31;
+            J = col >> 5;
+            lw = cc >> 3;
+            h = cc & 1;
+            j8 = (cc & 7) >> 1;
+          } else if constexpr (BITS == 2) {
+            const int cc = col & 63;
+            J = 2 * (col >> 6) + ((cc & 3) >> 1);
+            lw = cc >> 4;
+            h = cc & 1;
+            j8 = (cc & 15) >> 2;
+          } else {
+            const int ch = col >> 4, cc = col & 15;
+            J = ch >> 1;
+            lw = cc >> 2;
+            h = ch & 1;
+            j8 = cc & 3;
+          }
+          const uint32_t hw = xw[((J * xcols + 2 * n) * 4 + lw) * 2 + h];
+          const uint32_t lwd = xw[((J * xcols + 2 * n + 1) * 4 + lw) * 2 + h];
+          const int xh = (int)(hw << (24 - 8 * j8)) >> 24, xl = (int)(lwd << (24 - 8 * j8)) >> 24;
+          xv = (float)(256 * xh + xl) * f;
+        }
+        c = fmaf(xv, d, c);
       }
-      named_bar_sync(1, kConsumerThreads);
-      for (int it = threadIdx.x; it < n_own_rows * a.mt; it += kConsumerThreads) {
-        const int i = it / a.mt, n = it - i * a.mt;
-        const int lo = max(o_ptr[i] - o_base, j0), hi = min(o_ptr[i + 1] - o_base, j0 + jn);
-        float c = epi[i * kMaxTok + n];
-        for (int j = lo; j < hi; ++j) c += cbuf[(j - j0) * a.mt + n];
-        epi[i * kMaxTok + n] = c;
-      }
+      epi[i * kMaxTok + n] = c;
     }
   }
   named_bar_sync(1, kConsumerThreads);
@@ -541,6 +598,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const float4* sx1 = sx + (2 * l + 1) * n_seg;
   const bool tok0 = 2 * l < a.mt, tok1 = 2 * l + 1 < a.mt;
   const uint32_t slice_g = (uint32_t)(warp * kSlice) >> a.gbytes_shift;   // first group of the slice in the tile
+  // integer path: lane (q, l) feeds B column q (token group 0) and 8 + q
+  // (group 1, tokens 4..7) and accumulates tokens l and 4 + l
+  const bool two = a.mt > 4;
+  const bool has_b0 = q < xcols, has_b1 = 8 + q < xcols;
+  const uint2* xi_lane0 = xb + q * 4 + l;
+  const uint2* xi_lane1 = xb + (8 + q) * 4 + l;
+  const bool toka = l < a.mt, tokb = 4 + l < a.mt;
+  const float4* sxa = sx + l * n_seg;
+  const float4* sxb = sx + (4 + l) * n_seg;
 
   int cs = 0;
   uint32_t cph = 0;
@@ -562,61 +628,135 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const char* arow0 = st + q * kPitch + warp * kSlice + 4 * l;
     const char* arow1 = arow0 + 8 * kPitch;
     const uint32_t slice_byte0 = kg * (uint32_t)kTileK + warp * kSlice;
-    const int J_slice = (int)(slice_byte0 >> 4) * G::MPW;
+    // scale and min of row q + 8r for group `gi` of this warp's slice
+    auto group_meta = [&](int r, uint32_t gi, float& sc, float& gm) {
+      const uint32_t* mr = r ? mrow1 : mrow0;
+      const uint32_t off = (r ? moff1 : moff0) + gi;
+      if constexpr (DQ) {
+        const uint32_t* sup = meta + 2 * kTileRows * mrw;
+        const uint32_t row = row_q + 8 * r;
+        const uint32_t sj = dq_div(row * NGR + g0 + slice_g + gi, a) - sup_lo;
+        const float2 ms = __half22float2(u2h2(sup[sj]));
+        const float2 mg = __half22float2(u2h2(sup[kMaxSupers + sj]));
+        const float csv = (float)((mr[off >> 2] >> ((off & 3) * 8)) & 0xFFu);
+        const float cgv = (float)((mr[kTileRows * mrw + (off >> 2)] >> ((off & 3) * 8)) & 0xFFu);
+        sc = __fadd_rn(__fmul_rn(csv, ms.x), ms.y);
+        gm = __fadd_rn(__fmul_rn(cgv, mg.x), mg.y);
+      } else {
+        sc = h2f((uint16_t)(mr[off >> 1] >> ((off & 1) * 16)));
+        gm = h2f((uint16_t)(mr[kTileRows * mrw + (off >> 1)] >> ((off & 1) * 16)));
+      }
+    };
     const int gseg0 = (int)(slice_byte0 >> 4) / SEG;
     constexpr int NSG = kSlice / 16 / SEG;  // scale segments per warp slice
+    if constexpr (CB) {
+      const int J_slice = (int)(slice_byte0 >> 4) * G::MPW;
 #pragma unroll
-    for (int sg = 0; sg < NSG; ++sg) {
-      if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) break;
-      // two independent accumulator chains per segment
-      float cc[2][4];
+      for (int sg = 0; sg < NSG; ++sg) {
+        if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) break;
+        // two independent accumulator chains per segment
+        float cc[2][4];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) cc[u][0] = cc[u][1] = cc[u][2] = cc[u][3] = 0.f;
+        for (int u = 0; u < 2; ++u) cc[u][0] = cc[u][1] = cc[u][2] = cc[u][3] = 0.f;
 #pragma unroll
-      for (int cj = 0; cj < SEG; ++cj) {
-        const int cb = (sg * SEG + cj) * 16;
-        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(arow0 + cb);
-        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(arow1 + cb);
-        uint32_t P0[G::PPW], P1[G::PPW];
-        expand<BITS, CB>(w0, lut_lane, P0);
-        expand<BITS, CB>(w1, lut_lane, P1);
-        const int J0 = J_slice + (sg * SEG + cj) * G::MPW;
+        for (int cj = 0; cj < SEG; ++cj) {
+          const int cb = (sg * SEG + cj) * 16;
+          const uint32_t w0 = *reinterpret_cast<const uint32_t*>(arow0 + cb);
+          const uint32_t w1 = *reinterpret_cast<const uint32_t*>(arow1 + cb);
+          uint32_t P0[G::PPW], P1[G::PPW];
+          expand_cb<BITS>(w0, lut_lane, P0);
+          expand_cb<BITS>(w1, lut_lane, P1);
+          const int J0 = J_slice + (sg * SEG + cj) * G::MPW;
 #pragma unroll
-        for (int m = 0; m < G::MPW; ++m) {
-          uint2 bf = make_uint2(0u, 0u);
-          if (has_b) bf = xb_lane[(J0 + m) * 4];
-          mma16816(cc[(cj * G::MPW + m) & 1], P0[2 * m], P1[2 * m], P0[2 * m + 1], P1[2 * m + 1], bf.x, bf.y);
+          for (int m = 0; m < G::MPW; ++m) {
+            uint2 bf = make_uint2(0u, 0u);
+            if (has_b) bf = xb_lane[(J0 + m) * 4];
+            mma16816(cc[(cj * G::MPW + m) & 1], P0[2 * m], P1[2 * m], P0[2 * m + 1], P1[2 * m + 1], bf.x, bf.y);
+          }
+        }
+        float c[4];
+#pragma unroll
+        for (int z = 0; z < 4; ++z) c[z] = cc[0][z] + cc[1][z];
+        // close: acc += (s f) (C - Xc) + (g + C_cb s) X for rows q, q+8
+        const float4 fx0 = tok0 ? sx0[gseg0 + sg] : zero4;
+        const float4 fx1 = tok1 ? sx1[gseg0 + sg] : zero4;
+        const uint32_t gi = (uint32_t)(sg * SEG * 16) >> a.gbytes_shift;   // group within the slice
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          float sc, gm;
+          group_meta(r, gi, sc, gm);
+          const float gp = fmaf(center, sc, gm);
+          acc[2 * r] = fmaf(sc * fx0.x, c[2 * r], fmaf(gp, fx0.y, acc[2 * r]));
+          acc[2 * r + 1] = fmaf(sc * fx1.x, c[2 * r + 1], fmaf(gp, fx1.y, acc[2 * r + 1]));
         }
       }
-      float c[4];
+    } else {
+      // integer path: per segment, s32 sums of code * x~ (hi and lo columns),
+      // closed as acc += s f (256 C_hi + C_lo) + g X for rows q, q+8 and
+      // tokens l (acc[0], acc[1]) and 4 + l (acc[2], acc[3])
+      const int ch_slice = (int)(slice_byte0 >> 4);
 #pragma unroll
-      for (int z = 0; z < 4; ++z) c[z] = cc[0][z] + cc[1][z];
-      // close: acc += (s f) (C - Xc) + (g + C_cb s) X for rows q, q+8
-      const float4 fx0 = tok0 ? sx0[gseg0 + sg] : zero4;
-      const float4 fx1 = tok1 ? sx1[gseg0 + sg] : zero4;
-      const uint32_t gi = (uint32_t)(sg * SEG * 16) >> a.gbytes_shift;   // group within the slice
+      for (int sg = 0; sg < NSG; ++sg) {
+        if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) break;
+        int ci[2][2][4];   // [token group][chain][fragment]
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t* mr = r ? mrow1 : mrow0;
-        const uint32_t off = (r ? moff1 : moff0) + gi;
-        float sc, gm;
-        if constexpr (DQ) {
-          const uint32_t* sup = meta + 2 * kTileRows * mrw;
-          const uint32_t row = row_q + 8 * r;
-          const uint32_t sj = dq_div(row * NGR + g0 + slice_g + gi, a) - sup_lo;
-          const float2 ms = __half22float2(u2h2(sup[sj]));
-          const float2 mg = __half22float2(u2h2(sup[kMaxSupers + sj]));
-          const float csv = (float)((mr[off >> 2] >> ((off & 3) * 8)) & 0xFFu);
-          const float cgv = (float)((mr[kTileRows * mrw + (off >> 2)] >> ((off & 3) * 8)) & 0xFFu);
-          sc = __fadd_rn(__fmul_rn(csv, ms.x), ms.y);
-          gm = __fadd_rn(__fmul_rn(cgv, mg.x), mg.y);
-        } else {
-          sc = h2f((uint16_t)(mr[off >> 1] >> ((off & 1) * 16)));
-          gm = h2f((uint16_t)(mr[kTileRows * mrw + (off >> 1)] >> ((off & 1) * 16)));
+        for (int g = 0; g < 2; ++g)
+#pragma unroll
+          for (int u = 0; u < 2; ++u) ci[g][u][0] = ci[g][u][1] = ci[g][u][2] = ci[g][u][3] = 0;
+#pragma unroll
+        for (int cj = 0; cj < SEG; ++cj) {
+          const int cb = (sg * SEG + cj) * 16;
+          const uint32_t w0 = *reinterpret_cast<const uint32_t*>(arow0 + cb);
+          const uint32_t w1 = *reinterpret_cast<const uint32_t*>(arow1 + cb);
+          const int ch = ch_slice + sg * SEG + cj;
+          constexpr int NM = BITS == 2 ? 2 : 1;   // MMAs per chunk
+#pragma unroll
+          for (int m = 0; m < NM; ++m) {
+            uint32_t A0, A1, A2, A3;
+            int J;
+            if constexpr (BITS == 4) {
+              A0 = w0 & 0x0F0F0F0Fu;
+              A1 = w1 & 0x0F0F0F0Fu;
+              A2 = (w0 >> 4) & 0x0F0F0F0Fu;
+              A3 = (w1 >> 4) & 0x0F0F0F0Fu;
+              J = ch;
+            } else if constexpr (BITS == 2) {
+              A0 = (w0 >> (4 * m)) & 0x03030303u;
+              A1 = (w1 >> (4 * m)) & 0x03030303u;
+              A2 = (w0 >> (4 * m + 2)) & 0x03030303u;
+              A3 = (w1 >> (4 * m + 2)) & 0x03030303u;
+              J = 2 * ch + m;
+            } else {
+              const bool odd = ch & 1;
+              A0 = odd ? 0u : w0;
+              A1 = odd ? 0u : w1;
+              A2 = odd ? w0 : 0u;
+              A3 = odd ? w1 : 0u;
+              J = ch >> 1;
+            }
+            const int u = (cj * NM + m) & 1;
+            const uint2 b0 = has_b0 ? xi_lane0[J * xcols * 4] : make_uint2(0u, 0u);
+            imma16832(ci[0][u], A0, A1, A2, A3, b0.x, b0.y);
+            if (two) {
+              const uint2 b1 = has_b1 ? xi_lane1[J * xcols * 4] : make_uint2(0u, 0u);
+              imma16832(ci[1][u], A0, A1, A2, A3, b1.x, b1.y);
+            }
+          }
         }
-        const float gp = fmaf(center, sc, gm);
-        acc[2 * r] = fmaf(sc * fx0.x, c[2 * r] - fx0.z, fmaf(gp, fx0.y, acc[2 * r]));
-        acc[2 * r + 1] = fmaf(sc * fx1.x, c[2 * r + 1] - fx1.z, fmaf(gp, fx1.y, acc[2 * r + 1]));
+        const float4 fa = toka ? sxa[gseg0 + sg] : zero4;
+        const float4 fb = tokb ? sxb[gseg0 + sg] : zero4;
+        const uint32_t gi = (uint32_t)(sg * SEG * 16) >> a.gbytes_shift;   // group within the slice
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          float sc, gm;
+          group_meta(r, gi, sc, gm);
+          const int va = 256 * (ci[0][0][2 * r] + ci[0][1][2 * r]) + (ci[0][0][2 * r + 1] + ci[0][1][2 * r + 1]);
+          acc[r] = fmaf(sc * fa.x, (float)va, fmaf(gm, fa.y, acc[r]));
+          if (two) {
+            const int vb = 256 * (ci[1][0][2 * r] + ci[1][1][2 * r]) + (ci[1][0][2 * r + 1] + ci[1][1][2 * r + 1]);
+            acc[2 + r] = fmaf(sc * fb.x, (float)vb, fmaf(gm, fb.y, acc[2 + r]));
+          }
+        }
       }
     }
     __syncwarp();
@@ -626,10 +766,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (last_kg || t0 + i + 1 == t1) {
       // ---- flush row block rb: reduce the 8 warps' k-slices through smem ----
       float* rw = red + warp * kTileRows * kMaxTok;
-      rw[q * kMaxTok + 2 * l] = acc[0];
-      rw[q * kMaxTok + 2 * l + 1] = acc[1];
-      rw[(q + 8) * kMaxTok + 2 * l] = acc[2];
-      rw[(q + 8) * kMaxTok + 2 * l + 1] = acc[3];
+      if constexpr (CB) {
+        rw[q * kMaxTok + 2 * l] = acc[0];
+        rw[q * kMaxTok + 2 * l + 1] = acc[1];
+        rw[(q + 8) * kMaxTok + 2 * l] = acc[2];
+        rw[(q + 8) * kMaxTok + 2 * l + 1] = acc[3];
+      } else {
+        rw[q * kMaxTok + l] = acc[0];
+        rw[(q + 8) * kMaxTok + l] = acc[1];
+        rw[q * kMaxTok + 4 + l] = acc[2];
+        rw[(q + 8) * kMaxTok + 4 + l] = acc[3];
+      }
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
       named_bar_sync(1, kConsumerThreads);
       const int t = threadIdx.x;                 // t < 128: (row t/8, token t%8)
@@ -756,7 +903,7 @@ size_t fixed_smem(const ts_qweight& w, const Plan& p, int mt) {
          (size_t)p.max_owned_rows * gemv::kMaxTok * 4 +
          (size_t)gemv::kConsumerWarps * gemv::kTileRows * gemv::kMaxTok * 4 +
          (size_t)(p.max_owned_rows + 4) * 4 + (size_t)gemv::kOutCap * 8 + (size_t)(p.max_owned_rows + 4) * 4 +
-         (size_t)gemv::kCbuf * 4 + 2 * gemv::kMaxStages * 8 + 64;
+         2 * gemv::kMaxStages * 8 + 64;
 }
 
 size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024 / gemv::kCtasPerSm - (gemv::kCtasPerSm - 1) * 1024); }
@@ -886,7 +1033,6 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.seg_chunks = p.seg_chunks;
   a.gpt = p.gpt;
   a.max_owned_rows = p.max_owned_rows;
-  a.center = 0.f;  // uniform grids use raw codes; codebooks set their midpoint in-kernel
   a.gbytes_shift = ilog2((int64_t)w.group_size * w.bits / 8);
   a.dq_shift = -1;
   if (w.dq_group_size > 0 && (w.dq_group_size & (w.dq_group_size - 1)) == 0) a.dq_shift = ilog2(w.dq_group_size);
