@@ -173,6 +173,7 @@ struct Args {
   uint32_t tiles;      // row_blocks * kgroups
   uint32_t kgroups;    // tiles per row block
   uint32_t grid;
+  uint32_t quantum;    // tiles per unit of the CTA ranges (1, or kgroups: whole row blocks)
   int stages;          // ring depth
   int stage_bytes;     // packed rows + metadata of one stage
   int meta_row_words;  // 32-bit words per metadata row slot (per array)
@@ -228,8 +229,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const int mrw = a.meta_row_words;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t U = a.tiles, GR = a.grid;
-  const uint32_t t0 = (uint32_t)(U * blockIdx.x / GR), t1 = (uint32_t)(U * (blockIdx.x + 1) / GR);
+  // CTA b owns units [UQ b / G, UQ (b+1) / G) of `quantum` tiles each
+  const uint64_t Q = a.quantum, UQ = a.tiles / a.quantum, GR = a.grid;
+  const uint32_t t0 = (uint32_t)(UQ * blockIdx.x / GR * Q), t1 = (uint32_t)(UQ * (blockIdx.x + 1) / GR * Q);
   const uint32_t KG = a.kgroups;
   const uint32_t NGR = (uint32_t)a.q.n_groups;
 
@@ -801,8 +803,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int old = *s_flag;
         const uint64_t u0 = (uint64_t)rb * KG;
         int pieces = 1;
-        for (uint32_t cc = 1, prev = cta_of(u0, U, GR); cc < KG; ++cc) {
-          const uint32_t w = cta_of(u0 + cc, U, GR);
+        for (uint32_t cc = 1, prev = cta_of(u0 / Q, UQ, GR); cc < KG; ++cc) {
+          const uint32_t w = cta_of((u0 + cc) / Q, UQ, GR);
           pieces += w != prev;
           prev = w;
         }
@@ -810,10 +812,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           __threadfence();
           float sum = 0.f;
           for (uint32_t cc = 0, prev = 0xFFFFFFFFu; cc < KG; ++cc) {
-            const uint32_t pc = cta_of(u0 + cc, U, GR);
+            const uint32_t pc = cta_of((u0 + cc) / Q, UQ, GR);
             if (pc == prev) continue;
             prev = pc;
-            const uint32_t pfirst = (uint32_t)((U * pc / GR) / KG);
+            const uint32_t pfirst = (uint32_t)((UQ * pc / GR * Q) / KG);
             if (t < kTileRows * kMaxTok)
               sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) + t);
           }
@@ -848,7 +850,7 @@ int ilog2(int64_t v) {
 }
 
 struct Plan {
-  uint32_t tiles, kgroups, grid;
+  uint32_t tiles, kgroups, grid, quantum;
   int n_chunks, seg_chunks, gpt, meta_row_words, stage_bytes, max_owned_rows;
   bool meta_bulk;   // metadata rows are 16-byte multiples: 2-D copies into dense row slots
 };
@@ -879,6 +881,20 @@ Plan make_plan(const ts_qweight& w) {
   const uint32_t rbs = (uint32_t)((w.rows + gemv::kTileRows - 1) / gemv::kTileRows);
   p.tiles = rbs * p.kgroups;
   p.grid = std::max<uint32_t>(1, std::min<uint32_t>((uint32_t)sm_count() * gemv::kCtasPerSm, p.tiles));
+  // Row blocks of several tiles: hand out whole row blocks when that costs at
+  // most two tiles of imbalance on the busiest CTA. A row block split between
+  // CTAs is finished through global partial sums, a fence and an atomic, whose
+  // latency under full HBM load costs more than that.
+  p.quantum = 1;
+  if (p.kgroups > 1) {
+    const uint32_t g_rb = std::min(p.grid, rbs);
+    const double avg = (double)p.tiles / p.grid;
+    const double max_whole = (double)((rbs + g_rb - 1) / g_rb) * p.kgroups;
+    if (max_whole - avg <= 2.0) {
+      p.quantum = p.kgroups;
+      p.grid = g_rb;
+    }
+  }
   p.n_chunks = (int)(w.padded_cols * w.bits / 128);
   p.seg_chunks = (int)std::min<int64_t>(4, gbytes / 16);
   p.gpt = (int)(gemv::kTileK / gbytes);
@@ -1027,6 +1043,7 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.tiles = p.tiles;
   a.kgroups = p.kgroups;
   a.grid = p.grid;
+  a.quantum = p.quantum;
   a.stage_bytes = p.stage_bytes;
   a.meta_row_words = p.meta_row_words;
   a.n_chunks = p.n_chunks;

@@ -256,6 +256,22 @@ def test_qlinear_mlp_shapes(shape):
         assert err <= TOL, (M, err)
 
 
+@pytest.mark.parametrize("rows,cols,bits,mode", [(256, 16384, 4, "uniform"), (256, 16384, 4, "nf"),
+                                                 (200, 32768, 2, "uniform")])
+def test_qlinear_split_row_blocks(rows, cols, bits, mode):
+    """Few row blocks of four tiles each: the decode kernel splits row blocks
+    between CTAs and finishes them through the workspace partial sums."""
+    import tensorshrink_b200 as ts
+    d = _random_layer(rows, cols, bits=bits, gs=128, mode=mode, dq=False, seed=rows + bits, frac=0.001)
+    ql = ts.QuantLinear.from_device_quant(d)
+    W = goap.dequantize(d.to_quantized_tensor())
+    for M in (1, 5, 8):
+        x = torch.randn(M, cols).to(torch.bfloat16)
+        y = ql(x.cuda()).float().cpu().numpy()
+        err = goap.max_rel_error(y, x.float().numpy() @ W.T)
+        assert err <= TOL, (M, err)
+
+
 def test_functional_api_unsorted_outliers_and_fp32():
     import tensorshrink_b200 as ts
     from tensorshrink_b200.kernels import fused_quantized_linear
