@@ -697,6 +697,84 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       // closed as acc += s f (256 C_hi + C_lo) + g X for rows q, q+8 and
       // tokens l (acc[0], acc[1]) and 4 + l (acc[2], acc[3])
       const int ch_slice = (int)(slice_byte0 >> 4);
+      // unpack of chunk `ch` (words w0, w1 of rows q, q+8) into the A operand of MMA m
+      auto unpack = [&](uint32_t w0, uint32_t w1, int ch, int m, uint32_t& A0, uint32_t& A1, uint32_t& A2,
+                        uint32_t& A3, int& J) {
+        if constexpr (BITS == 4) {
+          A0 = w0 & 0x0F0F0F0Fu;
+          A1 = w1 & 0x0F0F0F0Fu;
+          A2 = (w0 >> 4) & 0x0F0F0F0Fu;
+          A3 = (w1 >> 4) & 0x0F0F0F0Fu;
+          J = ch;
+        } else if constexpr (BITS == 2) {
+          A0 = (w0 >> (4 * m)) & 0x03030303u;
+          A1 = (w1 >> (4 * m)) & 0x03030303u;
+          A2 = (w0 >> (4 * m + 2)) & 0x03030303u;
+          A3 = (w1 >> (4 * m + 2)) & 0x03030303u;
+          J = 2 * ch + m;
+        } else {
+          const bool odd = ch & 1;
+          A0 = odd ? 0u : w0;
+          A1 = odd ? 0u : w1;
+          A2 = odd ? w0 : 0u;
+          A3 = odd ? w1 : 0u;
+          J = ch >> 1;
+        }
+      };
+      constexpr int NM = BITS == 2 ? 2 : 1;   // MMAs per chunk
+      if (a.mt == 1) {
+        // One token: lanes (q, 0) hold each segment's integer sum for rows q,
+        // q+8; lane l then closes segments l, l+4, ... (no duplicated scale
+        // decode), and the four lanes' partials are added at the flush.
+        int va[2][NSG];
+#pragma unroll
+        for (int sg = 0; sg < NSG; ++sg) {
+          va[0][sg] = va[1][sg] = 0;
+          if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) continue;
+          int c4[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int cj = 0; cj < SEG; ++cj) {
+            const int cb = (sg * SEG + cj) * 16;
+            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(arow0 + cb);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(arow1 + cb);
+#pragma unroll
+            for (int m = 0; m < NM; ++m) {
+              uint32_t A0, A1, A2, A3;
+              int J;
+              unpack(w0, w1, ch_slice + sg * SEG + cj, m, A0, A1, A2, A3, J);
+              const uint2 b0 = has_b0 ? xi_lane0[J * xcols * 4] : make_uint2(0u, 0u);
+              imma16832(c4, A0, A1, A2, A3, b0.x, b0.y);
+            }
+          }
+          va[0][sg] = 256 * c4[0] + c4[1];
+          va[1][sg] = 256 * c4[2] + c4[3];
+        }
+#pragma unroll
+        for (int s0 = 0; s0 < NSG; s0 += 4) {
+          int v0 = 0, v1 = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (s0 + u < NSG) {
+              const int t0v = __shfl_sync(0xffffffffu, va[0][s0 + u], lane & ~3);
+              const int t1v = __shfl_sync(0xffffffffu, va[1][s0 + u], lane & ~3);
+              if (l == u) {
+                v0 = t0v;
+                v1 = t1v;
+              }
+            }
+          }
+          const int sg = s0 + l;
+          if (ok && sg < NSG && slice_byte0 + sg * SEG * 16 < (uint32_t)a.q.row_bytes) {
+            const float4 fa = sx[gseg0 + sg];
+            const uint32_t gi = (uint32_t)(sg * SEG * 16) >> a.gbytes_shift;
+            float sc, gm;
+            group_meta(0, gi, sc, gm);
+            acc[0] = fmaf(sc * fa.x, (float)v0, fmaf(gm, fa.y, acc[0]));
+            group_meta(1, gi, sc, gm);
+            acc[1] = fmaf(sc * fa.x, (float)v1, fmaf(gm, fa.y, acc[1]));
+          }
+        }
+      } else {
 #pragma unroll
       for (int sg = 0; sg < NSG; ++sg) {
         if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) break;
@@ -711,31 +789,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           const uint32_t w0 = *reinterpret_cast<const uint32_t*>(arow0 + cb);
           const uint32_t w1 = *reinterpret_cast<const uint32_t*>(arow1 + cb);
           const int ch = ch_slice + sg * SEG + cj;
-          constexpr int NM = BITS == 2 ? 2 : 1;   // MMAs per chunk
 #pragma unroll
           for (int m = 0; m < NM; ++m) {
             uint32_t A0, A1, A2, A3;
             int J;
-            if constexpr (BITS == 4) {
-              A0 = w0 & 0x0F0F0F0Fu;
-              A1 = w1 & 0x0F0F0F0Fu;
-              A2 = (w0 >> 4) & 0x0F0F0F0Fu;
-              A3 = (w1 >> 4) & 0x0F0F0F0Fu;
-              J = ch;
-            } else if constexpr (BITS == 2) {
-              A0 = (w0 >> (4 * m)) & 0x03030303u;
-              A1 = (w1 >> (4 * m)) & 0x03030303u;
-              A2 = (w0 >> (4 * m + 2)) & 0x03030303u;
-              A3 = (w1 >> (4 * m + 2)) & 0x03030303u;
-              J = 2 * ch + m;
-            } else {
-              const bool odd = ch & 1;
-              A0 = odd ? 0u : w0;
-              A1 = odd ? 0u : w1;
-              A2 = odd ? w0 : 0u;
-              A3 = odd ? w1 : 0u;
-              J = ch >> 1;
-            }
+            unpack(w0, w1, ch, m, A0, A1, A2, A3, J);
             const int u = (cj * NM + m) & 1;
             const uint2 b0 = has_b0 ? xi_lane0[J * xcols * 4] : make_uint2(0u, 0u);
             imma16832(ci[0][u], A0, A1, A2, A3, b0.x, b0.y);
@@ -760,6 +818,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           }
         }
       }
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
@@ -774,6 +833,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         rw[(q + 8) * kMaxTok + 2 * l] = acc[2];
         rw[(q + 8) * kMaxTok + 2 * l + 1] = acc[3];
       } else {
+        if (a.mt == 1) {   // the four lanes of a row pair hold partials of token 0
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
+          }
+        }
         rw[q * kMaxTok + l] = acc[0];
         rw[(q + 8) * kMaxTok + l] = acc[1];
         rw[q * kMaxTok + 4 + l] = acc[2];
