@@ -69,13 +69,19 @@ constexpr int kCtasPerSm = TS_GEMV_CPS;      // resident CTAs per SM (grid = SMs
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
 constexpr int kTileRows = 16;
-constexpr int kTileK = 2048;                       // packed bytes per row per tile
+#ifndef TS_GEMV_TILEK
+#define TS_GEMV_TILEK 2048
+#endif
+constexpr int kTileK = TS_GEMV_TILEK;              // packed bytes per row per tile
 constexpr int kSlice = kTileK / kConsumerWarps;    // 128 bytes per warp per row
 constexpr int kPitch = kTileK + 16;                // smem row pitch (conflict-free)
 constexpr int kMaxStages = 6;
 constexpr int kMaxTok = 8;
 constexpr int kMaxSupers = 64;                     // double-quant super-groups per tile
-constexpr int kOutCap = 2048;                      // outliers preloaded per CTA (more: read in place)
+#ifndef TS_GEMV_OUTCAP
+#define TS_GEMV_OUTCAP 2048
+#endif
+constexpr int kOutCap = TS_GEMV_OUTCAP;                      // outliers preloaded per CTA (more: read in place)
 
 template <int BITS>
 struct Geo {

@@ -7,4 +7,7 @@
 #define TS_GEMV_NS gemv_v2
 #define TS_GEMV_CW 8
 #define TS_GEMV_CPS 2
+// 512 outliers preloaded per CTA (more are read in place) so that the
+// activations of a 14336-column down projection fit half an SM
+#define TS_GEMV_OUTCAP 512
 #include "qgemv.cu"

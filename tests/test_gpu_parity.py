@@ -272,6 +272,21 @@ def test_qlinear_split_row_blocks(rows, cols, bits, mode):
         assert err <= TOL, (M, err)
 
 
+@pytest.mark.parametrize("mode", ["uniform", "nf"])
+def test_qlinear_many_outliers(mode):
+    """2% outliers: a CTA's outlier slice exceeds the preloaded part, the rest
+    is read in place."""
+    import tensorshrink_b200 as ts
+    d = _random_layer(2048, 4096, bits=4, gs=128, mode=mode, dq=False, seed=77, frac=0.02)
+    ql = ts.QuantLinear.from_device_quant(d)
+    W = goap.dequantize(d.to_quantized_tensor())
+    for M in (1, 3, 8):
+        x = torch.randn(M, 4096).to(torch.bfloat16)
+        y = ql(x.cuda()).float().cpu().numpy()
+        err = goap.max_rel_error(y, x.float().numpy() @ W.T)
+        assert err <= TOL, (M, err)
+
+
 def test_functional_api_unsorted_outliers_and_fp32():
     import tensorshrink_b200 as ts
     from tensorshrink_b200.kernels import fused_quantized_linear
