@@ -171,19 +171,24 @@ def gemv_flops(blocks, M):
 # prefill: BASELINE configs[2] layer at M = 2048 on the tensor-core kernel
 # ---------------------------------------------------------------------------
 
-def prefill_measure(device, reps=20, M=2048, rows=8192, cols=8192):
+def lloyd2_layer(device, rows, cols, seed=777):
+    import tensorshrink_b200 as ts
+    w = student_t_cuda((rows, cols), seed, device)
+    d = ts.quantize_device(w, bits=2, group_size=64, outlier_frac=0.001, companded=True)
+    del w
+    return ts.QuantLinear.from_device_quant(d)
+
+
+def prefill_measure(device, reps=20, M=2048, rows=8192, cols=8192, ql=None):
     """TFLOP/s of one [rows, cols] 2-bit Lloyd-Max g64 (+0.1% outliers) layer at
     M tokens (bf16). Each launch is timed alone between CUDA events on the
     launching stream, with L2 flushed (a 256 MB write) before it."""
     import torch
-    import tensorshrink_b200 as ts
     from tensorshrink_b200 import _C, kernels
 
     _, tc_peak, peak_kind = peaks()
-    w = student_t_cuda((rows, cols), 777, device)
-    d = ts.quantize_device(w, bits=2, group_size=64, outlier_frac=0.001, companded=True)
-    del w
-    ql = ts.QuantLinear.from_device_quant(d)
+    if ql is None:
+        ql = lloyd2_layer(device, rows, cols)
     qw = ql.qweight()
     x = torch.randn(M, cols, device=device).to(torch.bfloat16)
     out = torch.empty(M, rows, device=device, dtype=torch.bfloat16)
@@ -262,6 +267,84 @@ def quantize_measure(device, reps=3, rows=28672, cols=8192):
         "library_launches_per_call": int(launches),
         "projected_s_for_68.45B_params": round(68.45e9 * 2 / (gbs * 1e9), 2),
     }
+
+
+def prefill_sweep(device, reps=10):
+    """Config 3 across its token counts and shapes: TFLOP/s per (shape, M)."""
+    import torch
+    _, tc_peak, _ = peaks()
+    out = []
+    for rows, cols in ((8192, 8192), (28672, 8192), (8192, 28672)):
+        ql = lloyd2_layer(device, rows, cols, seed=rows + cols)
+        for M in (256, 2048, 8192):
+            r = prefill_measure(device, reps=reps, M=M, rows=rows, cols=cols, ql=ql)
+            out.append({"shape": [rows, cols], "M": M, "TFLOP/s": r["value"],
+                        "ms_per_launch": r["ms_per_launch"], "frac": round(r["value"] / tc_peak, 4)})
+        del ql
+        torch.cuda.empty_cache()
+    return {"workload": "lloyd2_g64_outlier0.001 prefill, bf16, L2 flushed before each launch",
+            "peak": tc_peak, "unit": "TFLOP/s", "points": out}
+
+
+def graph_time_ms(fn, device, reps):
+    """ms per call of `fn` replayed from a CUDA graph, CUDA events around
+    `reps` replays."""
+    import torch
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize(device)
+    return s.elapsed_time(e) / reps
+
+
+def decode_sweep(device, blocks, reps=50):
+    """Config 2 at M in {1, 8, 32, 64} (the bench MLP blocks, bf16) and
+    config 1 (32 distinct [4096, 4096] 4-bit g128 double-quant NF4 layers with
+    0.1% outliers, fp16 activations, M in {1, 16}): packed-weight GB/s of the
+    layers' algorithmic bytes, each a CUDA graph of one pass over weights
+    larger than L2."""
+    import torch
+    import tensorshrink_b200 as ts
+    hbm_peak, _, _ = peaks()
+    res = {"unit": "GB/s", "peak": hbm_peak, "config2_mlp_bf16": [], "config1_nf4_dq_fp16": []}
+    for M in (1, 8, 32, 64):
+        x = torch.randn(M, HIDDEN, device=device).to(torch.bfloat16)
+        ms = graph_time_ms(lambda: mlp_step(blocks, x), device, reps)
+        b = step_bytes(blocks, M)
+        res["config2_mlp_bf16"].append({"M": M, "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
+                                        "ms_per_step": round(ms, 4), "frac": round(b / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+                                        "tokens_per_s": round(M / (ms * 1e-3), 1)})
+    layers = []
+    for i in range(32):
+        w = student_t_cuda((4096, 4096), 5000 + i, device)
+        layers.append(ts.QuantLinear.from_device_quant(
+            ts.quantize_device(w, bits=4, group_size=128, outlier_frac=0.001, double_quant=True, nf_quant=True)))
+        del w
+    for M in (1, 16):
+        x = torch.randn(M, 4096, device=device).to(torch.float16)
+
+        def run():
+            for ql in layers:
+                ql(x)
+        ms = graph_time_ms(run, device, reps)
+        b = sum(ql.packed_nbytes() + 2 * M * (ql.in_features + ql.out_features) for ql in layers)
+        res["config1_nf4_dq_fp16"].append({"M": M, "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
+                                           "us_per_layer": round(ms * 1e3 / len(layers), 3),
+                                           "frac": round(b / (ms * 1e-3) / 1e9 / hbm_peak, 4)})
+    del layers
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -382,6 +465,9 @@ def run_ours(args, rank, world, device):
 
     prefill = prefill_measure(device) if not args.no_prefill else None
     quant = quantize_measure(device) if not args.no_prefill else None
+    sweeps = None
+    if not args.no_sweeps:
+        sweeps = {"decode": decode_sweep(device, blocks), "prefill": prefill_sweep(device)}
 
     out = None
     if rank == 0:
@@ -431,6 +517,7 @@ def run_ours(args, rank, world, device):
             "cpu_baseline": cpu,
             "prefill": prefill,
             "quantize": quant,
+            "sweeps": sweeps,
         }
     return out
 
@@ -532,6 +619,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-sweeps", action="store_true", help="skip the per-config M sweeps")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()

@@ -48,7 +48,8 @@ typedef enum ts_status {
   TS_ERR_INVALID = -1,     /* bad argument (shape, pointer, alignment) */
   TS_ERR_UNSUPPORTED = -2, /* valid but not covered (bit width, dtype) */
   TS_ERR_CUDA = -3,        /* a CUDA runtime call failed */
-  TS_ERR_WORKSPACE = -4    /* workspace missing or too small */
+  TS_ERR_WORKSPACE = -4,   /* workspace missing or too small */
+  TS_ERR_TIMEOUT = -5      /* a bounded wait in a kernel ran out (ts_qlinear_status) */
 } ts_status;
 
 /* One quantized weight matrix as resident on the device (QuantLinear's
@@ -105,16 +106,39 @@ TS_API int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M
  * same arguments minus the workspace. The decode kernel's scratch lives in a
  * fixed per-device array of ts_qlinear_noalloc_max_scratch() bytes (512 KiB)
  * inside the library, for callers that cannot allocate device memory. A
- * weight whose ts_qlinear_workspace_size() exceeds that returns
- * TS_ERR_UNSUPPORTED. The first call on each device resolves the array's
- * address and must happen before any stream capture. Calls that may overlap
- * on one device race on the shared array and must be serialized.
+ * call that takes the decode kernel (fewer than 65 tokens, or a layout the
+ * tensor-core kernel does not cover) with a weight whose
+ * ts_qlinear_workspace_size() exceeds that returns TS_ERR_UNSUPPORTED. The
+ * first call on each device loads the array there and must happen before
+ * any stream capture. Calls that may overlap on one device race on the
+ * shared array and must be serialized.
  */
 TS_API size_t ts_qlinear_noalloc_max_scratch(void);
 
 TS_API int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtype, int64_t M,
                int64_t x_row_stride, const void* bias, int bias_dtype, void* out,
                int out_dtype, int64_t out_row_stride, void* stream);
+
+/*
+ * Device error status of the qlinear kernels. Every barrier wait inside the
+ * kernels is bounded (2 s); a wait that runs out makes the kernel unwind
+ * (its results are then invalid) and records a code in the workspace's flag
+ * (decode kernel) or in a per-device flag (tensor-core kernel). This call
+ * synchronizes `stream`, reads both flags and returns TS_OK when neither is
+ * set, else TS_ERR_TIMEOUT with the codes in ts_last_error(). With
+ * clear != 0 it also resets the flags and the workspace's row-block
+ * counters, so the workspace is usable again. workspace == NULL checks the
+ * ts_qlinear_noalloc scratch array instead. No counterpart in the reference
+ * (its Triton kernels have no waits).
+ */
+TS_API int ts_qlinear_status(void* workspace, size_t workspace_bytes, int clear, void* stream);
+
+/* Test hook: the next qlinear kernel launch on the calling thread runs with
+ * its copy producer disabled and every barrier wait limited to
+ * `wait_limit_ns` (at most 2 s), so its first waits run out and the kernel
+ * reports TS_ERR_TIMEOUT through ts_qlinear_status. Nothing faults or hangs:
+ * the kernel returns within a few wait limits. */
+TS_API int ts_test_inject_stall(uint64_t wait_limit_ns);
 
 /* Standalone outlier correction into an fp32 result:
  *   out[m, row[k]] += x[m, col[k]] * delta[k]   for every k (any order).

@@ -22,7 +22,9 @@ _STATUS = {
     -2: NotImplementedError,  # TS_ERR_UNSUPPORTED
     -3: RuntimeError,        # TS_ERR_CUDA
     -4: RuntimeError,        # TS_ERR_WORKSPACE
+    -5: RuntimeError,        # TS_ERR_TIMEOUT
 }
+TS_ERR_TIMEOUT = -5
 
 _vp = C.c_void_p
 _i64 = C.c_int64
@@ -72,6 +74,8 @@ _SIGNATURES = [
     ("ts_qlinear_noalloc_max_scratch", C.c_size_t, []),
     ("ts_qlinear_noalloc", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int,
                                      _vp, C.c_int, _i64, _vp]),
+    ("ts_qlinear_status", C.c_int, [_vp, C.c_size_t, C.c_int, _vp]),
+    ("ts_test_inject_stall", C.c_int, [C.c_uint64]),
     ("ts_apply_outlier_correction", C.c_int, [_vp, _i64, _i64, _i64, _vp, C.c_int, _i64, _vp, _vp,
                                               _vp, _i64, _vp]),
     ("ts_dequantize_weight", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, C.c_int, _vp]),

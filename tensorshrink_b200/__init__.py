@@ -37,7 +37,7 @@ __version__ = "0.1.0"
 
 __all__ = [
     "QuantizedTensor", "DeviceQuant", "quantize_tensor", "dequantize_tensor", "quantize_tensor_adaptive",
-    "quantize_device", "dequantize_device", "relative_error", "QuantLinear", "quantize_module", "DEFAULT_SKIP_PATTERNS",
+    "quantize_device", "quantize_device_adaptive", "dequantize_device", "relative_error", "QuantLinear", "quantize_module", "DEFAULT_SKIP_PATTERNS",
     "T5_EXTRA_SKIP_PATTERNS", "suggest_max_dequant_rows", "quantize_tensor_gpu",
     "quantize_tensor_gpu_adaptive", "quantize_module_gpu", "fused_quantized_linear",
     "apply_outlier_correction", "dequantize_weight",

@@ -494,18 +494,22 @@ class LayerBitStats:
 
 
 def budget_allocate_bits(stats: Sequence[LayerBitStats], budget_bytes: float) -> Dict[str, int]:
-    """Greedy 4 -> 8-bit upgrades by error reduction per byte
-    (codec.py:997-1033)."""
-    bits = {s.name: 4 for s in stats}
-    remaining = budget_bytes - sum(s.bytes4 for s in stats)
-    cands: List[Tuple[float, str, int]] = []
-    for s in stats:
-        extra, gain = s.bytes8 - s.bytes4, s.err4 - s.err8
-        if extra > 0 and gain > 0:
-            cands.append((gain / extra, s.name, extra))
-    cands.sort(key=lambda c: c[0], reverse=True)
-    for _, name, extra in cands:
-        if extra <= remaining:
-            bits[name] = 8
-            remaining -= extra
-    return bits
+    """Bit plan under a byte budget, tensorshrink codec.py:997-1033.
+
+    Every layer starts at 4 bits. The bytes left in the budget then buy
+    8-bit upgrades, cheapest error per byte first (ties broken by layer name,
+    larger first, as the reference's tuple sort does); an upgrade that no
+    longer fits is skipped and the next one is tried."""
+    plan = dict.fromkeys((s.name for s in stats), 4)
+    left = budget_bytes - sum(s.bytes4 for s in stats)
+
+    def worth(s: LayerBitStats) -> Tuple[float, str]:
+        return ((s.err4 - s.err8) / (s.bytes8 - s.bytes4), s.name)
+
+    upgradable = [s for s in stats if s.bytes8 > s.bytes4 and s.err4 > s.err8]
+    for s in sorted(upgradable, key=worth, reverse=True):
+        cost = s.bytes8 - s.bytes4
+        if cost <= left:
+            plan[s.name] = 8
+            left -= cost
+    return plan

@@ -16,6 +16,7 @@ namespace ts {
   namespace ns {                                                                                     \
   bool gemv_supported(const ts_qweight& w);                                                          \
   size_t gemv_workspace_size(const ts_qweight& w);                                                   \
+  size_t gemv_error_flag_offset();                                                                   \
   int gemv_max_tokens(const ts_qweight& w);                                                          \
   int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,        \
                const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,      \
@@ -53,6 +54,7 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
 // Token counts from this one up go to the tensor-core kernel (the GEMV
 // re-streams the weights once per 8 tokens).
 constexpr int64_t kQgemmMinTokens = 65;
+int qgemm_error_flag(int* code, bool clear, cudaStream_t stream);
 int run_dequant(const ts_qweight& w, void* out, int out_dtype, int64_t out_stride,
                 int apply_outliers, cudaStream_t stream);
 int run_outlier_atomic(float* out, int64_t M, int64_t out_stride, const void* x, int x_dtype,
@@ -68,6 +70,11 @@ int run_lloyd_standalone(const float* vals, int64_t n, int n_levels, int iters, 
 namespace {
 thread_local char g_err[1024] = "";
 thread_local int64_t g_launches = 0;
+// default limit of every bounded wait in the kernels
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
+// test stall requested by ts_test_inject_stall for the next launch on this thread
+thread_local bool g_stall_next = false;
+thread_local uint64_t g_stall_wait_ns = kDefaultWaitNs;
 
 struct DevInfo {
   int sms = 0;
@@ -100,6 +107,12 @@ void set_error(const char* fmt, ...) {
 }
 
 void count_launch(int n) { g_launches += n; }
+uint64_t wait_limit_ns() { return g_stall_next ? g_stall_wait_ns : kDefaultWaitNs; }
+bool take_test_stall() {
+  const bool s = g_stall_next;
+  g_stall_next = false;
+  return s;
+}
 int sm_count() { return dev_info().sms; }
 int max_smem_optin() { return dev_info().smem_optin; }
 
@@ -137,6 +150,13 @@ extern "C" {
 const char* ts_last_error(void) { return g_err; }
 
 const char* ts_version(void) { return "tensorshrink_b200 0.1.0 (sm_100a)"; }
+
+int ts_test_inject_stall(uint64_t wait_limit_ns) {
+  TS_REQUIRE(wait_limit_ns > 0 && wait_limit_ns <= kDefaultWaitNs, "wait limit must be in (0, 2 s]");
+  g_stall_next = true;
+  g_stall_wait_ns = wait_limit_ns;
+  return TS_OK;
+}
 
 int64_t ts_launch_count(int reset) {
   const int64_t v = g_launches;
@@ -308,24 +328,15 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 512u << 10;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
-
-// Address of this device's scratch array, resolved once per device with the
-// device current. The first call loads the module on that device, which a
-// stream capture does not allow: make it before capturing.
+// Device address of the current device's scratch array. The host-side name
+// of a __device__ array is only a stand-in, so the address is asked of the
+// runtime on every call (cheap once the module is loaded; no stale pointer
+// survives a context reset). The first call on a device loads the module
+// there, which a stream capture does not allow: make it before capturing.
 int noalloc_scratch(void** out) {
-  int dev = -1;
-  TS_CUDA_TRY(cudaGetDevice(&dev));
-  TS_REQUIRE(dev >= 0 && dev < kMaxDevices, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> g(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    TS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  TS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+  *out = p;
   return TS_OK;
 }
 }  // namespace
@@ -341,11 +352,46 @@ extern "C" int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtyp
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != TS_OK) return rc;
-  const size_t need = gemv_supported(*w) ? gemv_workspace_size(*w) : 0;
+  // only the decode kernel uses scratch; the tensor-core kernel takes the
+  // calls of kQgemmMinTokens tokens and more whose layout it supports
+  const bool gemv_path = !(M >= kQgemmMinTokens && qgemm_supported(*w, x, x_row_stride)) && gemv_supported(*w);
+  const size_t need = gemv_path ? gemv_workspace_size(*w) : 0;
   TS_UNSUPPORTED(need <= kNoAllocScratchBytes,
                  "ts_qlinear_noalloc: weight of %lld rows needs %zu bytes of scratch, above the "
                  "fixed %zu; use ts_qlinear with a caller workspace",
                  (long long)w->rows, need, kNoAllocScratchBytes);
   return ts_qlinear(w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
                     out_row_stride, scratch, kNoAllocScratchBytes, stream);
+}
+
+// ---- device error status -------------------------------------------------------
+extern "C" int ts_qlinear_status(void* workspace, size_t workspace_bytes, int clear, void* stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = reinterpret_cast<char*>(workspace);
+  if (ws == nullptr) {
+    void* p = nullptr;
+    int rc = noalloc_scratch(&p);
+    if (rc != TS_OK) return rc;
+    ws = reinterpret_cast<char*>(p);
+    workspace_bytes = kNoAllocScratchBytes;
+  }
+  const size_t flag_off = gemv_v1::gemv_error_flag_offset();
+  TS_REQUIRE(workspace_bytes >= flag_off + 256, "workspace of %zu bytes is smaller than any GEMV workspace",
+             workspace_bytes);
+  int gemv_code = 0, gemm_code = 0;
+  TS_CUDA_TRY(cudaMemcpyAsync(&gemv_code, ws + flag_off, sizeof(int), cudaMemcpyDeviceToHost, st));
+  TS_CUDA_TRY(cudaStreamSynchronize(st));
+  int rc = qgemm_error_flag(&gemm_code, clear != 0, st);
+  if (rc != TS_OK) return rc;
+  if (gemv_code == 0 && gemm_code == 0) return TS_OK;
+  if (clear && gemv_code != 0) {
+    // the flag, and the row-block counters a CTA that gave up may have left
+    // non-zero (partial sums need no reset: each slot is written before it is read)
+    TS_CUDA_TRY(cudaMemsetAsync(ws + flag_off, 0, workspace_bytes - flag_off, st));
+    TS_CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  set_error("a bounded wait on the device ran out (decode kernel code %d, tensor-core kernel code %d); "
+            "the outputs of the calls since the last status check are not valid",
+            gemv_code, gemm_code);
+  return TS_ERR_TIMEOUT;
 }

@@ -54,6 +54,12 @@ void count_launch(int n = 1);
   } while (0)
 
 int sm_count();            // SMs of the current device (cached per device)
+// Limit of every bounded barrier wait in the kernels (2 s unless a test
+// stall asked for less), and whether the next launch is a test stall (its
+// copy producer issues nothing, so the first waits run out; see
+// ts_test_inject_stall). take_test_stall() consumes the request.
+uint64_t wait_limit_ns();
+bool take_test_stall();
 int max_smem_optin();      // opt-in shared memory per block of the current device
 
 inline bool is_aligned(const void* p, size_t a) {

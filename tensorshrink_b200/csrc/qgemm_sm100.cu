@@ -47,7 +47,7 @@ constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
 constexpr int kTmemCols = 512;
 constexpr int kAStageCols = kBK / 2;   // 64 16-bit values per lane = 32 columns
 
-__device__ int g_err;           // wait-timeout flag (diagnostic)
+__device__ int g_err;           // wait-timeout flag, read and cleared by ts_qlinear_status
 
 struct Args {
   QW q;
@@ -63,6 +63,8 @@ struct Args {
   int meta_groups;   // groups per metadata block (8 fp16 or 16 code bytes = 16 B)
   int gs_shift;      // log2(group_size)
   int dq_shift;      // log2(dq_group_size), or -1 when it is not a power of two
+  uint64_t wait_ns;  // limit of every barrier wait
+  int stall;         // test hook: the producer issues no copies, so the first waits run out
 };
 
 // ---- dequantization of 8-column chunks ----------------------------------------
@@ -244,7 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 1;
   uint64_t* m_full = tempty + 1;
   uint64_t* m_empty = m_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m_empty + 2);
+  uint64_t* mma_drain = m_empty + 2;   // the MMA issuer's final commit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   float* cbs = reinterpret_cast<float*>(tmem_slot + 4);   // codebook copy (<= 256 floats)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -258,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(tfull, 1);
     mbar_init(tempty, kEpiWarps * 32);
+    mbar_init(mma_drain, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(m_full + i, 1);
       mbar_init(m_empty + i, kDqWarps);
@@ -287,29 +291,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    if (lane == 0 && !a.stall) {
       uint32_t mit = 0, ph = 0;
       int s = 0;
       bool ok = true;
+      uint32_t issued = 0;   // stages issued (ring position = issued % S)
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const int m0 = (tile % a.tblocks) * BT, n0 = (tile / a.tblocks) * kBW;
         for (int kb = 0, mk = 0; kb < KB; ++kb) {
           if (a.meta_tma && mk == 0) {
             const int ms = mit & 1;
-            if (!mbar_wait_hint(m_empty + ms, ((mit >> 1) & 1) ^ 1, &g_err, 17)) { ok = false; break; }
+            if (!mbar_wait_hint(m_empty + ms, ((mit >> 1) & 1) ^ 1, &g_err, 17, a.wait_ns)) { ok = false; break; }
             mbar_arrive_expect_tx(m_full + ms, kMSlotBytes);
             unsigned char* slot = sM + (size_t)ms * kMSlotBytes;
             tma_load_2d(slot, &smap, (kb / spm) * a.meta_groups, n0, m_full + ms);
             tma_load_2d(slot + kBW * 16, &gmap, (kb / spm) * a.meta_groups, n0, m_full + ms);
             ++mit;
           }
-          if (!mbar_wait_hint(empty + s, ph ^ 1, &g_err, 11)) { ok = false; break; }
+          if (!mbar_wait_hint(empty + s, ph ^ 1, &g_err, 11, a.wait_ns)) { ok = false; break; }
           mbar_arrive_expect_tx(ld_full + s, kXStageBytes + kCStageBytes);
           tma_load_2d(sX + (size_t)s * kXStageBytes, &xmap, kb * kBK, m0, ld_full + s);
           tma_load_2d(sC + (size_t)s * kCStageBytes, &cmap, kb * kCodeBytes, n0, ld_full + s);
+          ++issued;
           if (++s == S) { s = 0; ph ^= 1; }
           if (++mk == spm) mk = 0;
         }
+      }
+      {
+        // let the copies in flight land before the CTA exits (after another
+        // role's timeout nobody else waits for them; normally they have landed)
+        for (uint32_t k = issued > (uint32_t)S ? issued - S : 0; k < issued; ++k)
+          mbar_wait_hint(ld_full + (k % S), (k / S) & 1, nullptr, 0, a.wait_ns);
+        for (uint32_t k = mit > 2 ? mit - 2 : 0; k < mit; ++k)
+          mbar_wait_hint(m_full + (k & 1), (k >> 1) & 1, nullptr, 0, a.wait_ns);
       }
     }
   } else if (warp == 1) {
@@ -326,10 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int t_local = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t_local) {
-        if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12)) { ok = false; break; }
+        if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12, a.wait_ns)) { ok = false; break; }
         tc_fence_after();
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13) || !mbar_wait_hint(a_full + s, ph, &g_err, 13)) {
+          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13, a.wait_ns) || !mbar_wait_hint(a_full + s, ph, &g_err, 13, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -345,6 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) umma_commit(tfull);
       }
+      // every MMA issued (also those of a tile abandoned after a timeout) has
+      // finished before the TMEM is freed
+      umma_commit(mma_drain);
+      mbar_wait_hint(mma_drain, 0, nullptr, 0, a.wait_ns);
     }
   } else if (warp < kFirstDqWarp) {
     // ---------------- epilogue ----------------
@@ -353,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
       const int64_t m0 = (int64_t)(tile % a.tblocks) * BT;
       const int64_t n = (int64_t)(tile / a.tblocks) * kBW + quad * 32 + lane;   // this thread's weight row
-      if (!mbar_wait_hint(tfull, t_local & 1, &g_err, 14)) break;
+      if (!mbar_wait_hint(tfull, t_local & 1, &g_err, 14, a.wait_ns)) break;
       tc_fence_after();
       const bool nvalid = n < q.rows;
       const float bias = (a.bias && nvalid) ? load_f(a.bias, a.bias_dtype, n) : 0.f;
@@ -441,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Waits for the current metadata block and releases it without using it
     // (a block that holds none of this group's stages).
     auto pass_block = [&]() -> bool {
-      if (!mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) return false;
+      if (!mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18, a.wait_ns)) return false;
       __syncwarp();
       if (lane == 0) mbar_arrive(m_empty + (mit & 1));
       ++mit;
@@ -499,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // their last stage in it, so a release can never be counted toward
           // an older use of the slot.
           if (cmk < kDqGroups &&
-              !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18)) { ok = false; break; }
+              !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18, a.wait_ns)) { ok = false; break; }
           const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
           const int ib = ((cmk << 6) + 32 * half) >> a.gs_shift;   // group of c0 within the block
 #pragma unroll
@@ -530,8 +548,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float2 sg[2];
         if (valid) decode(row_ng, kb, rawc, sg);
 
-        if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15) ||
-            !mbar_wait_hint(ld_full + cs, cph, &g_err, 16)) { ok = false; break; }
+        if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15, a.wait_ns) ||
+            !mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
         const unsigned char* crow = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes + half * (kCodeBytes / 2);
         uint32_t cw[kCodeBytes / 8];
         if (kCodeBytes / 2 >= 16) {
@@ -604,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 static size_t qgemm_smem(int BT, int bits, int S) {
   const size_t stage = (size_t)BT * qgemm::kBK * 2 + (size_t)qgemm::kBW * qgemm::kBK * bits / 8;
-  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 8) * 8 + 16 + 256 * 4;
+  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 9) * 8 + 16 + 256 * 4;
 }
 
 static int max_stages(int BT) { return (qgemm::kTmemCols - BT) / qgemm::kAStageCols; }
@@ -708,6 +726,8 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   }
   a.gs_shift = 0;
   while ((1 << a.gs_shift) < w.group_size) ++a.gs_shift;
+  a.wait_ns = wait_limit_ns();
+  a.stall = take_test_stall() ? 1 : 0;
   a.dq_shift = -1;
   if (w.dq_group_size > 0 && (w.dq_group_size & (w.dq_group_size - 1)) == 0) {
     a.dq_shift = 0;
@@ -718,6 +738,21 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   if (w.bits == 2) return launch_bits<2>(cb, xt, BT, maps, a, grid, smem, stream);
   if (w.bits == 4) return launch_bits<4>(cb, xt, BT, maps, a, grid, smem, stream);
   return launch_bits<8>(cb, xt, BT, maps, a, grid, smem, stream);
+}
+
+// Wait-timeout flag of the tensor-core kernel on the current device: returns
+// its value (0 = no timeout) and zeroes it when `clear` is set.
+int qgemm_error_flag(int* code, bool clear, cudaStream_t stream) {
+  int v = 0;
+  TS_CUDA_TRY(cudaMemcpyFromSymbolAsync(&v, qgemm::g_err, sizeof(int), 0, cudaMemcpyDeviceToHost, stream));
+  TS_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (clear && v != 0) {
+    const int zero = 0;
+    TS_CUDA_TRY(cudaMemcpyToSymbolAsync(qgemm::g_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream));
+    TS_CUDA_TRY(cudaStreamSynchronize(stream));
+  }
+  *code = v;
+  return TS_OK;
 }
 
 }  // namespace ts

@@ -175,7 +175,9 @@ struct Args {
   int64_t out_stride;
   float* partials;     // [grid][2][kTileRows][kMaxTok]
   int* counters;       // [row blocks]
-  int* err;            // wait-timeout flag
+  int* err;            // wait-timeout flag (read back by ts_qlinear_status)
+  uint64_t wait_ns;    // limit of every barrier wait
+  int stall;           // test hook: the producer issues no copies, so the first waits run out
   uint32_t tiles;      // row_blocks * kgroups
   uint32_t kgroups;    // tiles per row block
   uint32_t grid;
@@ -230,6 +232,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   int* s_flag = reinterpret_cast<int*>(bars + 2 * kMaxStages);
+  // set by the first wait that runs out: every role stops waiting and
+  // unwinds (the producer first lets its copies in flight land)
+  volatile int* s_abort = s_flag + 1;
   // per-stage metadata region (after the packed rows): plain: scale rows,
   // gmin rows; DQ: scale codes, gmin codes, scale supers, gmin supers
   const int mrw = a.meta_row_words;
@@ -246,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       mbar_init(full + i, a.meta_bulk ? 1 : 1 + 32);   // expect_tx arrival (+ 32 async-copy arrivals)
       mbar_init(empty + i, kConsumerWarps);
     }
+    *s_abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -253,11 +259,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   // ------------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
     pdl_launch_dependents();
+    if (a.stall) return;
     uint32_t rb = t0 / KG, kg = t0 - rb * KG;
     int s = 0;
     uint32_t ph = 0;          // phase of the ring pass that stage s belongs to
+    uint32_t issued = 0;
     for (uint32_t i = 0; t0 + i < t1; ++i) {
-      if (i >= (uint32_t)S && !mbar_wait_hint(empty + s, ph ^ 1, a.err, 1)) break;
+      // warp-uniform decisions: every lane takes part in the __syncwarp below
+      if (i >= (uint32_t)S && !__all_sync(0xffffffffu, mbar_wait_hint(empty + s, ph ^ 1, a.err, 1, a.wait_ns))) {
+        *s_abort = 1;
+        break;
+      }
+      if (__any_sync(0xffffffffu, *s_abort != 0)) break;
       char* st = stages + s * a.stage_bytes;
       uint32_t* meta = reinterpret_cast<uint32_t*>(st + kTileRows * kPitch);
       const uint32_t row0 = rb * kTileRows;
@@ -329,12 +342,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         cp_async_arrive(full + s);
       }
+      ++issued;
       if (++kg == KG) {
         kg = 0;
         ++rb;
       }
       if (++s == S) { s = 0; ph ^= 1; }
     }
+    // let the copies still in flight (the last S issues at most) land before
+    // this CTA's shared memory goes away: after a timeout the consumers stop
+    // waiting for them (in a normal run these phases have completed already)
+    for (uint32_t k = issued > (uint32_t)S ? issued - S : 0; k < issued; ++k)
+      mbar_wait_hint(full + (k % S), (k / S) & 1, nullptr, 0, a.wait_ns);
     return;
   }
 
@@ -620,7 +639,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint32_t cph = 0;
   for (uint32_t i = 0; t0 + i < t1; ++i) {
     const int s = cs;
-    const bool ok = mbar_wait_hint(full + s, cph, a.err, 2);
+    // warp-uniform: the MMAs below need every lane; after any role's timeout
+    // the remaining tiles are skipped without waiting
+    bool ok = !__any_sync(0xffffffffu, *s_abort != 0);
+    if (ok && !__all_sync(0xffffffffu, mbar_wait_hint(full + s, cph, a.err, 2, a.wait_ns))) {
+      ok = false;
+      *s_abort = 1;
+    }
     if (++cs == S) { cs = 0; cph ^= 1; }
     const char* st = stages + s * a.stage_bytes;
     const uint32_t* meta = reinterpret_cast<const uint32_t*>(st + kTileRows * kPitch);
@@ -1076,6 +1101,10 @@ static size_t gemv_partials_bytes() {
   return align_up((size_t)sm_count() * kLayoutCtasPerSm * 2 * gemv::kTileRows * gemv::kMaxTok * sizeof(float), 256);
 }
 
+// Byte offset of the wait-timeout flag in the workspace; the row-block
+// counters start 256 bytes later.
+size_t gemv_error_flag_offset() { return gemv_partials_bytes(); }
+
 size_t gemv_workspace_size(const ts_qweight& w) {
   const int64_t rbs = (w.rows + gemv::kTileRows - 1) / gemv::kTileRows;
   return gemv_partials_bytes() + 256 + align_up((size_t)rbs * sizeof(int), 256);
@@ -1111,6 +1140,8 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   char* ws = reinterpret_cast<char*>(workspace);
   a.partials = reinterpret_cast<float*>(ws);
   a.err = reinterpret_cast<int*>(ws + gemv_partials_bytes());
+  a.wait_ns = wait_limit_ns();
+  a.stall = take_test_stall() ? 1 : 0;
   a.counters = reinterpret_cast<int*>(ws + gemv_partials_bytes() + 256);
   a.tiles = p.tiles;
   a.kgroups = p.kgroups;

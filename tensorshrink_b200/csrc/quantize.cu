@@ -30,8 +30,7 @@
 namespace ts {
 
 int run_lloyd(const float* vals, int64_t n, int n_levels, int iters, float* out, uint16_t* out16,
-              char* ws, cudaStream_t stream, size_t off_state, size_t off_sums, size_t off_cnts,
-              size_t off_mm);
+              char* ws, cudaStream_t stream, size_t off_state, size_t off_mm);
 
 namespace qz {
 
@@ -684,12 +683,15 @@ __global__ void row_ptr_kernel(const int32_t* idx, int64_t k, int64_t cols, int6
 }
 
 // ---- Lloyd-Max fit (codec.py:320-361) -----------------------------------------------
-// Sums are accumulated as 64-bit fixed point (exact, order independent) so
-// the fit is deterministic; the fixed-point scale is chosen from max|v|.
+// The reference accumulates each level's values with index_add_, which on CPU
+// adds them one after the other in element order in float32. The fit here
+// does exactly that (one thread per level walking the values in order), so
+// the fitted levels are bit-identical to the reference's CPU fit on the same
+// sample.
 struct LloydState {
   float lo, hi;
-  int shift;         // fixed-point fraction bits
   int n_levels;
+  int pad;
   float cent[256];   // current centroids (unsorted positions, like the reference)
   float mids[256];   // decision boundaries of the sorted centroids
   int order[256];    // sorted position -> centroid index
@@ -719,7 +721,8 @@ __global__ void lloyd_minmax_kernel(const float* v, int64_t n, float* mm /* [2*b
   }
 }
 
-// Sort the current centroids (stable rank sort) and derive mids.
+// Sort the current centroids (stable rank sort, as torch.sort orders equal
+// keys by position) and derive the decision boundaries (a + b) / 2.
 __device__ void lloyd_prepare(LloydState* s) {
   const int L = s->n_levels;
   __shared__ float sc[256];
@@ -757,64 +760,59 @@ __global__ void lloyd_init_kernel(const float* mm, int nblk, int64_t n, int n_le
         s->cent[i] = i < half ? __fadd_rn(lo, __fmul_rn(step, (float)i))
                               : __fsub_rn(hi, __fmul_rn(step, (float)(L - i - 1)));
     }
-    const float amax = fmaxf(fabsf(lo), fabsf(hi));
-    int e = 0;
-    frexpf(fmaxf(amax, 1e-30f), &e);              // amax < 2^e
-    int nb = 0;
-    while ((1ll << nb) < n) ++nb;                 // n <= 2^nb
-    s->shift = max(0, min(60, 62 - e - nb));
   }
   __syncthreads();
   lloyd_prepare(s);
 }
 
-__global__ void lloyd_accum_kernel(const float* v, int64_t n, const LloydState* s,
-                                   unsigned long long* sums, unsigned long long* cnts) {
+// All `iters` Lloyd iterations in one block of 256 threads. Per iteration the
+// values stream through shared memory in chunks: every thread assigns a
+// share of the chunk (searchsorted over the boundaries, left side, then the
+// sorted position's centroid index), then thread c walks the whole chunk in
+// order and adds the values assigned to centroid c to its float32 sum and
+// count. New centroid = sum / count; an empty centroid keeps its value.
+constexpr int kLloydChunk = 4096;
+__global__ void __launch_bounds__(256) lloyd_fit_kernel(const float* v, int64_t n, LloydState* s, int iters) {
+  __shared__ float cv[kLloydChunk];
+  __shared__ uint8_t ca[kLloydChunk];
   __shared__ float mids[256];
   __shared__ int order[256];
-  __shared__ unsigned long long ls[256], lc[256];
   const int L = s->n_levels;
-  for (int i = threadIdx.x; i < L; i += blockDim.x) {
-    mids[i] = s->mids[i];
-    order[i] = s->order[i];
-    ls[i] = 0;
-    lc[i] = 0;
-  }
-  __syncthreads();
-  const float scale = ldexpf(1.f, s->shift);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float x = v[i];
-    int lo = 0, hi = L - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (mids[mid] < x) lo = mid + 1; else hi = mid;
+  const int c = threadIdx.x;
+  for (int it = 0; it < iters; ++it) {
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+      mids[i] = s->mids[i];
+      order[i] = s->order[i];
     }
-    const int c = order[lo];
-    const long long fx = __double2ll_rn((double)x * (double)scale);
-    atomicAdd(&ls[c], (unsigned long long)fx);
-    atomicAdd(&lc[c], 1ull);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < L; i += blockDim.x) {
-    if (lc[i]) {
-      atomicAdd(&sums[i], ls[i]);
-      atomicAdd(&cnts[i], lc[i]);
+    __syncthreads();
+    float sum = 0.f, cnt = 0.f;
+    for (int64_t base = 0; base < n; base += kLloydChunk) {
+      const int m = (int)i64min(kLloydChunk, n - base);
+      for (int j = threadIdx.x; j < m; j += blockDim.x) {
+        const float x = v[base + j];
+        int lo = 0, hi = L - 1;   // first boundary >= x (the count of boundaries below x)
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (mids[mid] < x) lo = mid + 1; else hi = mid;
+        }
+        cv[j] = x;
+        ca[j] = (uint8_t)order[lo];
+      }
+      __syncthreads();
+      if (c < L) {
+        for (int j = 0; j < m; ++j) {
+          const bool mine = ca[j] == c;
+          const float t = __fadd_rn(sum, cv[j]);
+          sum = mine ? t : sum;
+          cnt = mine ? __fadd_rn(cnt, 1.f) : cnt;
+        }
+      }
+      __syncthreads();
     }
+    if (c < L && cnt > 0.f) s->cent[c] = __fdiv_rn(sum, cnt);
+    __syncthreads();
+    lloyd_prepare(s);
   }
-}
-
-__global__ void lloyd_update_kernel(LloydState* s, unsigned long long* sums, unsigned long long* cnts) {
-  const int L = s->n_levels;
-  for (int i = threadIdx.x; i < L; i += blockDim.x) {
-    if (cnts[i]) {
-      const double sum = (double)(long long)sums[i] / ldexp(1.0, s->shift);
-      s->cent[i] = __fdiv_rn((float)sum, (float)cnts[i]);
-    }
-    sums[i] = 0;
-    cnts[i] = 0;
-  }
-  __syncthreads();
-  lloyd_prepare(s);
 }
 
 __global__ void lloyd_output_kernel(const LloydState* s, int n_levels, float* out, uint16_t* out16) {
@@ -856,7 +854,7 @@ __global__ void to_half_kernel(const float* src, int n, uint16_t* dst) {
 // ---- workspace layout ------------------------------------------------------------
 struct WsLayout {
   size_t gmin_raw, gmax_raw, hist1, hist2, sel, cta_hist, cta_info, lloyd_vals, lloyd_state,
-      lloyd_sums, lloyd_cnts, lloyd_mm, cb32, total;
+      lloyd_mm, cb32, total;
 };
 
 constexpr int kLloydBlocks = 296;
@@ -896,8 +894,6 @@ inline WsLayout layout(const ts_quant_params& p, int dtype) {
                             : 0;
   l.lloyd_vals = take(n_fit * 4);
   l.lloyd_state = take(sizeof(LloydState));
-  l.lloyd_sums = take(256 * 8);
-  l.lloyd_cnts = take(256 * 8);
   l.lloyd_mm = take(kLloydBlocks * 2 * 4);
   l.cb32 = take(256 * 4);
   l.total = o;
@@ -983,7 +979,7 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
     TS_LAUNCH_CHECK();
     float* cb32 = o.codebook_out ? o.codebook_out : reinterpret_cast<float*>(ws + L.cb32);
     const int rc = run_lloyd(vals, n_fit, n_levels, p.lloyd_iters, cb32, o.codebook_f16, ws, stream,
-                             L.lloyd_state, L.lloyd_sums, L.lloyd_cnts, L.lloyd_mm);
+                             L.lloyd_state, L.lloyd_mm);
     if (rc != TS_OK) return rc;
     cb_assign = cb32;
   }
@@ -1068,26 +1064,19 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
 }  // namespace qz
 
 int run_lloyd(const float* vals, int64_t n, int n_levels, int iters, float* out, uint16_t* out16,
-              char* ws, cudaStream_t stream, size_t off_state, size_t off_sums, size_t off_cnts,
-              size_t off_mm) {
+              char* ws, cudaStream_t stream, size_t off_state, size_t off_mm) {
   using namespace qz;
   TS_REQUIRE(n > 0, "lloyd_fit: no values");
   TS_REQUIRE(n_levels >= 1 && n_levels <= 256, "lloyd_fit: n_levels must be in [1, 256]");
   LloydState* s = reinterpret_cast<LloydState*>(ws + off_state);
-  auto* sums = reinterpret_cast<unsigned long long*>(ws + off_sums);
-  auto* cnts = reinterpret_cast<unsigned long long*>(ws + off_cnts);
   float* mm = reinterpret_cast<float*>(ws + off_mm);
-  TS_CUDA_TRY(cudaMemsetAsync(sums, 0, 256 * 8, stream));
-  TS_CUDA_TRY(cudaMemsetAsync(cnts, 0, 256 * 8, stream));
   const int blocks = (int)qz::i64min((n + 255) / 256, (int64_t)kLloydBlocks);
   lloyd_minmax_kernel<<<blocks, 256, 0, stream>>>(vals, n, mm);
   TS_LAUNCH_CHECK();
   lloyd_init_kernel<<<1, 256, 0, stream>>>(mm, blocks, n, n_levels, s);
   TS_LAUNCH_CHECK();
-  for (int it = 0; it < iters; ++it) {
-    lloyd_accum_kernel<<<blocks, 256, 0, stream>>>(vals, n, s, sums, cnts);
-    TS_LAUNCH_CHECK();
-    lloyd_update_kernel<<<1, 256, 0, stream>>>(s, sums, cnts);
+  if (iters > 0) {
+    lloyd_fit_kernel<<<1, 256, 0, stream>>>(vals, n, s, iters);
     TS_LAUNCH_CHECK();
   }
   lloyd_output_kernel<<<1, 256, 0, stream>>>(s, n_levels, out, out16);
@@ -1096,17 +1085,15 @@ int run_lloyd(const float* vals, int64_t n, int n_levels, int iters, float* out,
 }
 
 size_t lloyd_ws_size() {
-  return align_up(sizeof(qz::LloydState), 256) + 2 * 256 * 8 + align_up(qz::kLloydBlocks * 2 * 4, 256) + 1024;
+  return align_up(sizeof(qz::LloydState), 256) + align_up(qz::kLloydBlocks * 2 * 4, 256) + 1024;
 }
 
 int run_lloyd_standalone(const float* vals, int64_t n, int n_levels, int iters, float* out, char* ws,
                          size_t ws_bytes, cudaStream_t stream) {
   TS_REQUIRE(ws_bytes >= lloyd_ws_size(), "lloyd_fit: workspace too small");
   const size_t st = 0;
-  const size_t sums = align_up(sizeof(qz::LloydState), 256);
-  const size_t cnts = sums + 256 * 8;
-  const size_t mm = cnts + 256 * 8;
-  return run_lloyd(vals, n, n_levels, iters, out, nullptr, ws, stream, st, sums, cnts, mm);
+  const size_t mm = align_up(sizeof(qz::LloydState), 256);
+  return run_lloyd(vals, n, n_levels, iters, out, nullptr, ws, stream, st, mm);
 }
 
 size_t quantize_ws_size(const ts_quant_params& p, int dtype) { return qz::layout(p, dtype).total; }

@@ -156,7 +156,31 @@ class _Workspaces:
             return buf
 
 
+    def on_device(self, index: int) -> List[torch.Tensor]:
+        with self._lock:
+            return [b for b in self._all if b.device.index == index]
+
+
 _WORKSPACES = _Workspaces()
+
+
+def device_status(device: Optional[torch.device] = None, clear: bool = True) -> None:
+    """Raise RuntimeError if a bounded wait inside a qlinear kernel ran out
+    on `device` since the last check (`ts_qlinear_status` over every cached
+    workspace of the device). The call synchronizes the current stream; with
+    `clear` the flags and the workspaces' counters are reset, so later calls
+    run normally. A timed-out call's outputs are not valid."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    lib = _C.load()
+    with torch.cuda.device(dev):
+        stream = _stream_handle(dev)
+        bufs = _WORKSPACES.on_device(dev.index) + [None]   # None: the no-alloc scratch
+        for b in bufs:
+            if b is None:
+                rc = lib.ts_qlinear_status(None, 0, 1 if clear else 0, stream)
+            else:
+                rc = lib.ts_qlinear_status(b.data_ptr(), int(b.numel()), 1 if clear else 0, stream)
+            _C.check(rc, "ts_qlinear_status")
 
 
 def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor:

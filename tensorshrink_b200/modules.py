@@ -5,7 +5,10 @@ arguments, same registered buffers (names, dtypes, shapes, row-sorted
 outlier tables), so reference state_dicts load unchanged. The forward pass is
 one `ts_qlinear` call for fp16/bf16 activations at any M (decode GEMV or
 prefill GEMM chosen inside the library), with the outlier correction and bias
-fused. There is no CPU forward: CPU tensors raise.
+fused. CUDA tensors always run the sm_100a kernels (a missing library
+raises); a layer whose buffers and input are on the CPU runs the reference's
+CPU algorithm (chunked dequantize + F.linear, modules.py:752-804, 924-940),
+which never touches the GPU path.
 
 Differences from the reference that callers can see:
 * `cache`, `use_triton`, `fast_dequant`, `max_dequant_rows` are accepted and
@@ -306,10 +309,65 @@ class QuantLinear(nn.Module):
             dq_group_size=self.dq_group_size, outlier_row=self.outlier_row,
             outlier_col=self.outlier_col, outlier_delta=self.outlier_delta)
 
+    def _codes_rows(self, r0: int, r1: int) -> torch.Tensor:
+        """Integer codes [r1 - r0, padded_cols] of rows [r0, r1) (CPU)."""
+        pk = self.packed[r0:r1]
+        if self.bits == 8:
+            return pk
+        per = 8 // self.bits
+        shifts = torch.arange(per, dtype=torch.uint8) * self.bits
+        mask = (1 << self.bits) - 1
+        codes = (pk.unsqueeze(-1) >> shifts) & mask          # code j of byte b at [.., b, j]
+        return codes.reshape(r1 - r0, -1)[:, : self.padded_cols]
+
+    def _dequantize_rows_cpu(self, r0: int, r1: int, compute_dtype: torch.dtype) -> torch.Tensor:
+        """Rows [r0, r1) of W on the CPU, the reference's chunked dequant
+        (modules.py:752-804): codes (or codebook values) * scale + gmin in the
+        compute dtype when fast_dequant and the compute dtype is 16-bit, else
+        fp32; outlier positions get fp32(base) + delta, rounded once."""
+        n = r1 - r0
+        calc = compute_dtype if (self.fast_dequant and compute_dtype in (torch.float16, torch.bfloat16)) \
+            else torch.float32
+        s_full, g_full = self._scale_gmin_f32()
+        sc = s_full[r0:r1].to(calc).unsqueeze(-1)
+        gm = g_full[r0:r1].to(calc).unsqueeze(-1)
+        codes = self._codes_rows(r0, r1).reshape(n, self.n_groups, self.group_size)
+        if self.companded:
+            vals = self.codebook.to(calc)[codes.long()]
+        else:
+            vals = codes.to(calc)
+        w = (vals * sc + gm).reshape(n, self.padded_cols)[:, : self.cols].contiguous()
+        lo = int(self.outlier_row_ptr[r0])
+        hi = int(self.outlier_row_ptr[r1])
+        if hi > lo:
+            flat = w.view(-1)
+            idx = (self.outlier_row[lo:hi].long() - r0) * self.cols + self.outlier_col[lo:hi].long()
+            base = flat[idx].to(torch.float32)
+            flat[idx] = (base + self.outlier_delta[lo:hi].to(torch.float32)).to(calc)
+        return w.to(compute_dtype)
+
+    def _forward_cpu(self, x: torch.Tensor) -> torch.Tensor:
+        """The reference's CPU forward (modules.py:924-940): dequantize
+        `max_dequant_rows` rows at a time and F.linear each chunk."""
+        in_dtype = x.dtype
+        compute_dtype = torch.float32 if self.force_fp32_compute else in_dtype
+        x = x.to(compute_dtype)
+        bias = self.bias.to(compute_dtype) if self.bias is not None else None
+        step = max(1, int(self.max_dequant_rows))
+        outs = []
+        for r0 in range(0, self.rows, step):
+            r1 = min(r0 + step, self.rows)
+            b = bias[r0:r1] if bias is not None else None
+            outs.append(F.linear(x, self._dequantize_rows_cpu(r0, r1, compute_dtype), b))
+        out = outs[0] if len(outs) == 1 else torch.cat(outs, dim=-1)
+        return out.to(in_dtype) if out.dtype != in_dtype else out
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.device.type == "cpu" and self.packed.device.type == "cpu":
+            return self._forward_cpu(x)
         if not (x.is_cuda and self.packed.is_cuda):
-            raise RuntimeError("tensorshrink_b200 QuantLinear runs on CUDA only "
-                               f"(input on {x.device}, weights on {self.packed.device})")
+            raise RuntimeError("QuantLinear: input on {} and weights on {} (both must be on one CUDA "
+                               "device, or both on the CPU)".format(x.device, self.packed.device))
         in_dtype = x.dtype
         compute_dtype = torch.float32 if self.force_fp32_compute else in_dtype
         if compute_dtype in (torch.float16, torch.bfloat16):
@@ -377,22 +435,25 @@ class QuantLinear(nn.Module):
 # ---------------------------------------------------------------------------
 
 def _set_module_by_name(root: nn.Module, dotted_name: str, new_module: nn.Module) -> None:
-    parts = dotted_name.split(".")
-    obj = root
-    for p in parts[:-1]:
-        obj = getattr(obj, p)
-    setattr(obj, parts[-1], new_module)
+    """Replace the submodule at `dotted_name` (e.g. "layers.3.mlp.up_proj")."""
+    parent_name, _, leaf = dotted_name.rpartition(".")
+    parent = root.get_submodule(parent_name) if parent_name else root
+    setattr(parent, leaf, new_module)
 
 
 def _iter_target_linears(model: nn.Module, min_numel: int, skip_name_patterns: Iterable[str]):
-    pats = tuple(p.lower() for p in skip_name_patterns)
-    for name, module in model.named_modules():
-        if isinstance(module, nn.Linear) and not isinstance(module, QuantLinear):
-            if module.weight.numel() < min_numel:
-                continue
-            if any(p in name.lower() for p in pats):
-                continue
-            yield name, module
+    """(name, nn.Linear) pairs to quantize: plain Linear layers (not already
+    QuantLinear) with at least `min_numel` weights whose lower-cased name
+    contains none of the skip patterns (modules.py:1033-1051)."""
+    skip = [p.lower() for p in skip_name_patterns]
+
+    def eligible(name: str, mod: nn.Module) -> bool:
+        if type(mod) is QuantLinear or not isinstance(mod, nn.Linear):
+            return False
+        lname = name.lower()
+        return mod.weight.numel() >= min_numel and not any(p in lname for p in skip)
+
+    return [(n, m) for n, m in model.named_modules() if eligible(n, m)]
 
 
 def model_weight_bytes(model: nn.Module) -> int:

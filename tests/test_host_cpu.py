@@ -65,11 +65,25 @@ def test_to_quantized_tensor_roundtrip(golden, name):
                                qt.outlier_val[ref_order].astype(np.float32), rtol=2e-3, atol=1e-4)
 
 
-def test_cpu_forward_raises(golden):
+@pytest.mark.parametrize("name", golden_case_list())
+def test_cpu_forward_matches_reference(golden, name):
+    """A QuantLinear on the CPU runs the reference's CPU algorithm: its output
+    equals the reference QuantLinear.forward output bit for bit."""
+    c = load_case(golden, name)
+    bias = torch.from_numpy(c["bias"]) if "bias" in c else None
+    ql = QuantLinear(qt_from_case(c), bias=bias)
+    x = torch.from_numpy(c["x"]).to(getattr(torch, str(c["x_dtype"])))
+    y = ql(x)
+    assert y.dtype == x.dtype
+    np.testing.assert_array_equal(y.float().numpy(), c["y_cpu"].astype(np.float32))
+
+
+def test_cpu_forward_rejects_mixed_devices(golden):
     c = load_case(golden, "nf4_dq_g128")
     ql = QuantLinear(qt_from_case(c))
-    with pytest.raises(RuntimeError, match="CUDA"):
-        ql(torch.zeros(1, ql.in_features, dtype=torch.float16))
+    x = torch.zeros(1, ql.in_features, dtype=torch.float16, device="meta")
+    with pytest.raises(RuntimeError, match="CUDA device, or both on the CPU"):
+        ql(x)
 
 
 def test_state_dict_roundtrip_rebuilds_row_ptr(golden):
