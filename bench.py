@@ -130,10 +130,14 @@ def student_t_cuda(shape, seed, device):
     return w.to(torch.float16)
 
 
-def build_blocks(n_blocks, device, seed0=0):
-    """n_blocks MLP blocks of QuantLinear (4-bit g128 uniform + outliers)."""
+def build_blocks(n_blocks, device, seed0=0, world=1, rank=0):
+    """n_blocks MLP blocks of QuantLinear (4-bit g128 uniform + outliers).
+    With world > 1 each block is tensor-parallel: this rank keeps its
+    column shard of gate/up and its row shard of down (whole layers are
+    quantized identically on every rank, then cut)."""
     import torch
     import tensorshrink_b200 as ts
+    from tensorshrink_b200.decoder import ShardedProjection
     blocks = []
     for b in range(n_blocks):
         layers = []
@@ -141,24 +145,41 @@ def build_blocks(n_blocks, device, seed0=0):
             w = student_t_cuda(shape, seed0 + 10 * b + j, device)
             dq = ts.quantize_device(w, bits=4, group_size=128, outlier_frac=0.001, double_quant=False,
                                     nf_quant=False)
-            layers.append(ts.QuantLinear.from_device_quant(dq))
-            del w
+            ql = ts.QuantLinear.from_device_quant(dq)
+            del w, dq
+            layers.append(ql if world == 1 else ShardedProjection(ql, world, rank, "row" if j == 2 else "column"))
         blocks.append(layers)
     torch.cuda.synchronize(device)
     return blocks
 
 
-def mlp_step(blocks, x):
+def layer_of(p):
+    """The QuantLinear a block entry runs (itself, or a shard's local layer)."""
+    return getattr(p, "local", p)
+
+
+def mlp_step(blocks, x, world=1):
+    import torch
+    import torch.distributed as dist
     import torch.nn.functional as F
     for gate, up, down in blocks:
-        x = down(F.silu(gate(x)) * up(x))
+        m = F.silu(gate(x)) * up(x)
+        if world == 1:
+            x = down(m)
+        else:
+            y = down(m, torch.float32)          # this rank's partial sum
+            dist.all_reduce(y)
+            x = y.to(torch.bfloat16)
     return x
 
 
 def step_bytes(blocks, M):
+    """Algorithmic bytes of this rank's share of one step: packed weights and
+    metadata, plus its activations in and outputs out."""
     b = 0
     for layers in blocks:
-        for ql in layers:
+        for p in layers:
+            ql = layer_of(p)
             b += ql.packed_nbytes() + 2 * M * (ql.in_features + ql.out_features)
     return b
 
@@ -347,6 +368,50 @@ def decode_sweep(device, blocks, reps=50):
     return res
 
 
+def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32):
+    """the Llama-3-8B-shaped decoder (32 layers, per-layer
+    bits drawn from 2/4/8 with a fixed seed, g128 uniform + 0.1% outliers),
+    tensor-parallel over the `world` ranks. Decode: B sequences with `ctx`
+    tokens of context, one CUDA-graph step per token, `steps` steps timed
+    with CUDA events (max over ranks). Prefill: one 2048-token sequence.
+    Reports tokens/s and the aggregate packed-weight GB/s of all ranks."""
+    import torch
+    import torch.distributed as dist
+    from tensorshrink_b200.decoder import CUDAGraphDecoder, QuantDecoder, llama3_8b_config
+    cfg = llama3_8b_config(seed=0)
+    model = QuantDecoder(cfg, device, max_batch=max(batches), max_seq=2048)
+    packed = float(model.packed_nbytes())
+    if world > 1:
+        t = torch.tensor([packed], device=device, dtype=torch.float64)
+        dist.all_reduce(t)
+        packed = float(t.item())
+    g = torch.Generator(device=device).manual_seed(0)
+    res = {"workload": "llama3_8b_shaped_32L_bits_2_4_8_seeded_g128_uniform_outlier0.001",
+           "layer_bits": model.layer_bits, "packed_bytes_all_ranks": int(packed),
+           "parallelism": f"tp x{world}" if world > 1 else "single GPU",
+           "attention": "plain torch SDPA over a static bf16 KV cache (outside the measured path)",
+           "decode": []}
+    attn_len = ctx + steps + 8
+    for B in batches:
+        tokens = torch.randint(0, cfg.vocab, (B, ctx), device=device, generator=g)
+        first = model.prefill(tokens)
+        runner = CUDAGraphDecoder(model, B, attn_len=attn_len)
+        model.prefill(tokens)
+        runner.start(first, ctx)
+        ms = timed(runner.step, steps) / steps
+        res["decode"].append({"batch": B, "context": ctx, "ms_per_step": round(ms, 4),
+                              "tokens_per_s": round(B / (ms * 1e-3), 1),
+                              "packed_GB/s": round(packed / (ms * 1e-3) / 1e9, 1)})
+        del runner
+    tokens = torch.randint(0, cfg.vocab, (1, 2048), device=device, generator=g)
+    model.prefill(tokens)
+    ms = timed(lambda: model.prefill(tokens), 3) / 3
+    res["prefill_2048"] = {"ms": round(ms, 3), "tokens_per_s": round(2048 / (ms * 1e-3), 1)}
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -358,19 +423,19 @@ def run_ours(args, rank, world, device):
 
     torch.manual_seed(0)
     hbm_peak, _, peak_kind = peaks()
-    blocks = build_blocks(args.blocks, device)
+    blocks = build_blocks(args.blocks, device, world=world, rank=rank)
     M = args.M
     x0 = torch.randn(M, HIDDEN, device=device).to(torch.bfloat16)
     static_x = x0.clone()
 
     # ---- capture one step as a CUDA graph ----
     for _ in range(2):
-        mlp_step(blocks, static_x)
+        mlp_step(blocks, static_x, world)
     torch.cuda.synchronize(device)
     _C.launch_count(reset=True)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        static_y = mlp_step(blocks, static_x)
+        static_y = mlp_step(blocks, static_x, world)
     launches_per_step = _C.launch_count(reset=True)
 
     for _ in range(max(args.warmup, 3)):
@@ -412,19 +477,29 @@ def run_ours(args, rank, world, device):
             torch.cuda.synchronize(device)
     ms_per_step = ms / args.steps
     bytes_step = step_bytes(blocks, M)
-    value = world * bytes_step / (ms_per_step * 1e-3) / 1e9
+    if world > 1:
+        # whole-job bytes: every rank's shard (the shards partition the layers)
+        t = torch.tensor([float(bytes_step)], device=device, dtype=torch.float64)
+        dist.all_reduce(t)
+        bytes_job = float(t.item())
+    else:
+        bytes_job = float(bytes_step)
+    value = bytes_job / (ms_per_step * 1e-3) / 1e9
 
     # ---- dominant kernel: the GEMV launches alone, graph-replayed ----
-    gx = {HIDDEN: torch.randn(M, HIDDEN, device=device).to(torch.bfloat16),
-          INTER: torch.randn(M, INTER, device=device).to(torch.bfloat16)}
-    layers = [ql for blk in blocks for ql in blk]
+    layers = [p for blk in blocks for p in blk]
+    gx = {}
+    for p in layers:
+        k = layer_of(p).in_features
+        if k not in gx:
+            gx[k] = torch.randn(M, k, device=device).to(torch.bfloat16)
     kgraph = torch.cuda.CUDAGraph()
-    for ql in layers:
-        ql(gx[ql.in_features])
+    for p in layers:
+        p(gx[layer_of(p).in_features])
     torch.cuda.synchronize(device)
     with torch.cuda.graph(kgraph):
-        for ql in layers:
-            ql(gx[ql.in_features])
+        for p in layers:
+            p(gx[layer_of(p).in_features])
     for _ in range(3):
         kgraph.replay()
     reps = max(args.steps, 10)
@@ -439,7 +514,7 @@ def run_ours(args, rank, world, device):
 
     def e2e_step():
         xd.copy_(xh, non_blocking=True)
-        y = mlp_step(blocks, xd)
+        y = mlp_step(blocks, xd, world)
         yh.copy_(y, non_blocking=True)
 
     for _ in range(3):
@@ -455,23 +530,30 @@ def run_ours(args, rank, world, device):
     for _ in range(3):
         e2e_graph.replay()
     e2e_ms = timed(e2e_graph.replay, args.steps) / args.steps
-    e2e_val = world * bytes_step / (e2e_ms * 1e-3) / 1e9
-    eager_val = world * bytes_step / (eager_ms * 1e-3) / 1e9
+    e2e_val = bytes_job / (e2e_ms * 1e-3) / 1e9
+    eager_val = bytes_job / (eager_ms * 1e-3) / 1e9
 
     # correctness guard on the timed graph output (finite, non-trivial)
     graph.replay()
     torch.cuda.synchronize(device)
     assert torch.isfinite(static_y.float()).all(), "non-finite bench output"
 
-    prefill = prefill_measure(device) if not args.no_prefill else None
-    quant = quantize_measure(device) if not args.no_prefill else None
+    # single-GPU kernel studies: at N = 1 only
+    solo = world == 1
+    prefill = prefill_measure(device) if solo and not args.no_prefill else None
+    quant = quantize_measure(device) if solo and not args.no_prefill else None
     sweeps = None
-    if not args.no_sweeps:
+    if solo and not args.no_sweeps:
         sweeps = {"decode": decode_sweep(device, blocks), "prefill": prefill_sweep(device)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(blocks, M, budget_s=args.cpu_seconds)
+    del blocks, graph, kgraph, e2e_graph
+    torch.cuda.empty_cache()
+    decoder = decoder_measure(device, world, timed) if not args.no_decoder else None
 
     out = None
     if rank == 0:
-        cpu = cpu_baseline(blocks, M, budget_s=args.cpu_seconds) if world == 1 and not args.no_cpu else None
         out = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -481,7 +563,7 @@ def run_ours(args, rank, world, device):
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 5),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
             "dtype": "u4 codes x bf16 (fp32 accumulate)",
             "data": "synthetic (seeded Student-t(df=4) weights, N(0,1) activations)",
@@ -491,10 +573,11 @@ def run_ours(args, rank, world, device):
                 "bytes_per_step": bytes_step,
                 "l2": f"inputs larger than L2: {args.blocks} distinct MLP blocks "
                       f"({bytes_step / 1e6:.0f} MB packed) streamed per step",
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "parallelism": f"tp x{world} (gate/up column-parallel, down row-parallel + NCCL all-reduce "
+                               f"of fp32 partials)" if world > 1 else "single GPU",
                 "timing": "CUDA graph of one step, K replays between CUDA events, max over ranks",
             },
-            "tokens_per_s": round(world * M / (ms_per_step * 1e-3), 1),
+            "tokens_per_s": round(M / (ms_per_step * 1e-3), 1),
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(xh.numel() * xh.element_size()),
                     "d2h_bytes_per_step": int(yh.numel() * yh.element_size()),
@@ -518,6 +601,7 @@ def run_ours(args, rank, world, device):
             "prefill": prefill,
             "quantize": quant,
             "sweeps": sweeps,
+            "decoder": decoder,
         }
     return out
 
@@ -620,6 +704,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-sweeps", action="store_true", help="skip the per-config M sweeps")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the Llama-3-8B-shaped decoder")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()

@@ -149,6 +149,21 @@ TS_API int ts_apply_outlier_correction(float* out, int64_t M, int64_t N, int64_t
                                 const int32_t* row, const int32_t* col,
                                 const uint16_t* delta, int64_t n_outliers, void* stream);
 
+/* QuantLinear outlier tables from a container's outlier stream.
+ * Replaces the host decode of container.py:142-153 `_decode_outliers` plus
+ * the table build of modules.py:414-448, 649-715. Inputs: the weight
+ * (packed codes and metadata set; outlier fields ignored) and the stream as
+ * stored: row deltas and columns as unsigned 16- or 32-bit integers
+ * (index_bytes), values fp16, n entries, rows non-decreasing. Outputs
+ * (device): int32 rows (prefix sums of the deltas) and columns, fp16 deltas
+ * f16(value - (cb?[code] * scale + gmin)) in fp32 with the double-quant
+ * metadata reconstructed in fp32, and CSR offsets row_ptr[rows + 1].
+ * *bad_flag (device int) is set to 1 when an entry lies outside the weight. */
+TS_API int ts_outlier_tables_from_stream(const ts_qweight* w, const void* row_delta, const void* col,
+                                         int index_bytes, const uint16_t* val, int64_t n, int32_t* row_out,
+                                         int32_t* col_out, uint16_t* delta_out, int32_t* row_ptr_out,
+                                         int* bad_flag, void* stream);
+
 /* Dense reconstruction W[rows, cols] in `out_dtype`.
  * Replaces triton_kernels.py:1114-1186 `dequantize_weight` (which covers only
  * 4/8-bit; this covers 2/4/8 and the double-quantized metadata). With

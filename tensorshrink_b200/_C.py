@@ -78,6 +78,8 @@ _SIGNATURES = [
     ("ts_test_inject_stall", C.c_int, [C.c_uint64]),
     ("ts_apply_outlier_correction", C.c_int, [_vp, _i64, _i64, _i64, _vp, C.c_int, _i64, _vp, _vp,
                                               _vp, _i64, _vp]),
+    ("ts_outlier_tables_from_stream", C.c_int, [C.POINTER(TsQWeight), _vp, _vp, C.c_int, _vp, _i64, _vp, _vp,
+                                                _vp, _vp, _vp, _vp]),
     ("ts_dequantize_weight", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, C.c_int, _vp]),
     ("ts_quantize_workspace_size", C.c_size_t, [C.POINTER(TsQuantParams)]),
     ("ts_quantize_pack", C.c_int, [_vp, C.c_int, C.POINTER(TsQuantParams), C.POINTER(TsQuantOutputs),

@@ -12,6 +12,7 @@ from .codec import (
     dequantize_tensor,
     quantize_tensor_adaptive,
     quantize_device,
+    quantize_device_adaptive,
     dequantize_device,
     relative_error,
 )

@@ -49,11 +49,18 @@ int run_generic_qlinear(const ts_qweight& w, const void* x, int x_dtype, int64_t
                         int64_t x_stride, const void* bias, int bias_dtype, void* out,
                         int out_dtype, int64_t out_stride, cudaStream_t stream);
 bool qgemm_supported(const ts_qweight& w, const void* x, int64_t x_stride);
+size_t qgemm_workspace_extra(const ts_qweight& w, int64_t M, size_t counters_bytes_gemv);
+bool qgemm_split_fits(const ts_qweight& w, int64_t M, size_t counters_off, size_t ws_bytes);
 int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride, const void* bias,
-              int bias_dtype, void* out, int out_dtype, int64_t out_stride, cudaStream_t stream);
-// Token counts from this one up go to the tensor-core kernel (the GEMV
-// re-streams the weights once per 8 tokens).
+              int bias_dtype, void* out, int out_dtype, int64_t out_stride, void* workspace, size_t counters_off,
+              size_t ws_bytes, cudaStream_t stream);
+// Token counts from this one up always go to the tensor-core kernel.
 constexpr int64_t kQgemmMinTokens = 65;
+// From this one up they go there too when the workspace holds the split
+// plan's partial sums (the GEMV takes at most 8 tokens per pass over the
+// weights; the split tensor-core kernel reads the weights once for any M,
+// and is the faster of the two from three GEMV passes on).
+constexpr int64_t kSplitMinTokens = 17;
 int qgemm_error_flag(int* code, bool clear, cudaStream_t stream);
 int run_dequant(const ts_qweight& w, void* out, int out_dtype, int64_t out_stride,
                 int apply_outliers, cudaStream_t stream);
@@ -165,9 +172,13 @@ int64_t ts_launch_count(int reset) {
 }
 
 size_t ts_qlinear_workspace_size(const ts_qweight* w, int64_t M) {
-  (void)M;
   if (!w) return 0;
-  return gemv_supported(*w) ? gemv_workspace_size(*w) : 0;
+  const size_t head = gemv_v1::gemv_error_flag_offset() + 256;   // partial sums of the GEMV + error flag
+  const size_t base = gemv_supported(*w) ? std::max(gemv_workspace_size(*w), head) : head;
+  // split tensor-core plans serve calls of kSplitMinTokens tokens and more
+  const bool gemv_fits = gemv_supported(*w) && gemv_v1::gemv_max_tokens(*w) > 0;
+  const int64_t Ms = gemv_fits ? M : std::max<int64_t>(M, kSplitMinTokens);
+  return base + (Ms >= kSplitMinTokens ? qgemm_workspace_extra(*w, Ms, base - head) : 0);
 }
 
 int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M, int64_t x_row_stride,
@@ -185,9 +196,22 @@ int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M, int64
   TS_REQUIRE(w->n_outliers == 0 || w->outlier_row_ptr != nullptr,
              "qlinear needs the CSR outlier_row_ptr table");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (M >= kQgemmMinTokens && qgemm_supported(*w, x, x_row_stride))
-    return run_qgemm(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride, s);
-  if (gemv_supported(*w)) {
+  const size_t counters_off = gemv_v1::gemv_error_flag_offset() + 256;
+  if (qgemm_supported(*w, x, x_row_stride)) {
+    const bool split_ok = workspace != nullptr && qgemm_split_fits(*w, M, counters_off, workspace_bytes);
+    if (M >= kQgemmMinTokens || (M >= kSplitMinTokens && split_ok))
+      return run_qgemm(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride,
+                       split_ok ? workspace : nullptr, counters_off, workspace_bytes, s);
+  }
+  // activations too long for the decode kernel's shared-memory staging:
+  // the split tensor-core kernel when the workspace holds it, else the
+  // generic kernel below
+  const bool gemv_fits = gemv_supported(*w) && gemv_v1::gemv_max_tokens(*w) > 0;
+  if (!gemv_fits && qgemm_supported(*w, x, x_row_stride) && workspace != nullptr &&
+      qgemm_split_fits(*w, std::max<int64_t>(M, kSplitMinTokens), counters_off, workspace_bytes))
+    return run_qgemm(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride, workspace,
+                     counters_off, workspace_bytes, s);
+  if (gemv_fits) {
     TS_REQUIRE(workspace != nullptr, "workspace is NULL (size %zu needed)", gemv_workspace_size(*w));
     return run_gemv(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
                     out_row_stride, workspace, workspace_bytes, s);
@@ -355,6 +379,8 @@ extern "C" int ts_qlinear_noalloc(const ts_qweight* w, const void* x, int x_dtyp
   // only the decode kernel uses scratch; the tensor-core kernel takes the
   // calls of kQgemmMinTokens tokens and more whose layout it supports
   const bool gemv_path = !(M >= kQgemmMinTokens && qgemm_supported(*w, x, x_row_stride)) && gemv_supported(*w);
+  // (the fixed array is too small for the split tensor-core plan's partial
+  // sums, so 9..64-token calls take the decode kernel here)
   const size_t need = gemv_path ? gemv_workspace_size(*w) : 0;
   TS_UNSUPPORTED(need <= kNoAllocScratchBytes,
                  "ts_qlinear_noalloc: weight of %lld rows needs %zu bytes of scratch, above the "

@@ -31,6 +31,9 @@
 // TMEM), which is what bounds a design that stages both operands there.
 // Every wait is bounded in wall-clock time: on timeout the kernel records an
 // error flag and all roles unwind to the final barrier, where the TMEM is freed.
+#include <algorithm>
+#include <cmath>
+
 #include "sm100.cuh"
 
 namespace ts {
@@ -46,6 +49,7 @@ constexpr int kFirstDqWarp = 2 + kEpiWarps;
 constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
 constexpr int kTmemCols = 512;
 constexpr int kAStageCols = kBK / 2;   // 64 16-bit values per lane = 32 columns
+constexpr int kPrefetchStages = 32;    // L2 prefetch distance of the code stream
 
 __device__ int g_err;           // wait-timeout flag, read and cleared by ts_qlinear_status
 
@@ -65,6 +69,10 @@ struct Args {
   int dq_shift;      // log2(dq_group_size), or -1 when it is not a power of two
   uint64_t wait_ns;  // limit of every barrier wait
   int stall;         // test hook: the producer issues no copies, so the first waits run out
+  int split;         // CTAs take equal ranges of K-stages (tiles split between CTAs)
+  float* partials;   // split: [grid][2][128 rows][BT tokens] fp32
+  int* counters;     // split: one per tile, zero between calls
+  int prefetch_codes;  // L2-prefetch each item's code columns through cmap_wide
 };
 
 // ---- dequantization of 8-column chunks ----------------------------------------
@@ -221,16 +229,71 @@ __device__ __forceinline__ float outlier_value(const QW& q, const float* cbs, in
   return __fadd_rn(__fmul_rn(v, g.x), g.y) + __half2float(q.odelta[j]);
 }
 
+// ---- work items ----------------------------------------------------------------
+// A tile is 128 weight rows x BT tokens over the whole K. Without split, CTA b
+// takes tiles b, b + grid, ... whole. With split, the tiles' K-stages are laid
+// end to end (tile-major) and CTA b takes the contiguous range of units
+// [U b / G, U (b + 1) / G): every CTA gets the same number of stages, and a
+// tile whose stages span several CTAs is finished by the last of them to
+// arrive, from fp32 partial sums in the workspace (pieces added in CTA
+// order, so results do not depend on timing).
+struct Item {
+  int tile, k0, k1;   // stages [k0, k1) of the tile
+  int slot;           // partial-sum slot: 0 = the CTA's first item, 1 = any later one
+};
+
+struct ItemIter {
+  int next, end;
+  bool first;
+};
+
+__device__ __forceinline__ int split_unit_begin(int units, int cta, int grid) {
+  return (int)((int64_t)units * cta / grid);
+}
+
+__device__ __forceinline__ ItemIter items_begin(const Args& a, int ntiles) {
+  ItemIter it;
+  if (a.split) {
+    const int U = ntiles * a.kblocks;
+    it.next = split_unit_begin(U, blockIdx.x, gridDim.x);
+    it.end = split_unit_begin(U, blockIdx.x + 1, gridDim.x);
+  } else {
+    it.next = blockIdx.x;
+    it.end = ntiles;
+  }
+  it.first = true;
+  return it;
+}
+
+__device__ __forceinline__ bool items_next(const Args& a, ItemIter& it, Item& x) {
+  if (it.next >= it.end) return false;
+  if (a.split) {
+    x.tile = it.next / a.kblocks;
+    x.k0 = it.next - x.tile * a.kblocks;
+    x.k1 = min(a.kblocks, x.k0 + (it.end - it.next));
+    it.next += x.k1 - x.k0;
+  } else {
+    x.tile = it.next;
+    x.k0 = 0;
+    x.k1 = a.kblocks;
+    it.next += gridDim.x;
+  }
+  x.slot = it.first ? 0 : 1;
+  it.first = false;
+  return true;
+}
+
 // ---- the kernel -------------------------------------------------------------
 template <int BITS, bool CB, int XT, int BT>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
                  const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap gmap,
-                 const Args a) {
+                 const __grid_constant__ CUtensorMap cmap_wide, const Args a) {
   constexpr int kXStageBytes = BT * kBK * 2;
   constexpr int kCodeBytes = kBK * BITS / 8;              // per weight row per stage
   constexpr int kCStageBytes = kBW * kCodeBytes;
   constexpr int kMSlotBytes = 2 * kBW * 16;               // {scale, min} x [128 rows][16 B]
+  constexpr int kCW = BT >= 32 ? 32 : 16;                 // accumulator columns per TMEM load
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte aligned base by pointer arithmetic on the shared array itself, so
   // the compiler keeps the shared address space (ld.shared, not generic loads)
@@ -249,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_drain = m_empty + 2;   // the MMA issuer's final commit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   float* cbs = reinterpret_cast<float*>(tmem_slot + 4);   // codebook copy (<= 256 floats)
+  int* epi_flag = reinterpret_cast<int*>(cbs + 256);     // split: counter value seen by the epilogue
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const QW& q = a.q;
@@ -286,7 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;         // columns [0, BT): accumulator; then S A-stages
   const int ntiles = a.tblocks * a.wblocks;
-  const int KB = a.kblocks;
   const int spm = a.meta_groups * q.group_size / kBK;   // stages per metadata block
 
   if (warp == 0) {
@@ -296,10 +359,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       bool ok = true;
       uint32_t issued = 0;   // stages issued (ring position = issued % S)
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % a.tblocks) * BT, n0 = (tile / a.tblocks) * kBW;
-        for (int kb = 0, mk = 0; kb < KB; ++kb) {
-          if (a.meta_tma && mk == 0) {
+      ItemIter it = items_begin(a, ntiles);
+      Item x;
+      while (ok && items_next(a, it, x)) {
+        const int m0 = (x.tile % a.tblocks) * BT, n0 = (x.tile / a.tblocks) * kBW;
+        // Code columns reach L2 ahead of their stages in 256-byte row
+        // segments, kPrefetchStages ahead: the per-stage boxes are only 16-64
+        // bytes per row, and fetched from DRAM one stage at a time they leave
+        // the pipeline waiting on DRAM latency.
+        const int c_end = x.k1 * kCodeBytes;
+        int c_pf = (x.k0 * kCodeBytes) & ~255;   // next segment to prefetch
+        for (int kb = x.k0; kb < x.k1; ++kb) {
+          if (a.prefetch_codes) {
+            const int c_want = min(c_end, (kb + kPrefetchStages) * kCodeBytes);
+            for (; c_pf < c_want; c_pf += 256) tma_prefetch_2d(&cmap_wide, c_pf, n0);
+          }
+          if (a.meta_tma && (kb == x.k0 || kb % spm == 0)) {
+            // the metadata block holding stage kb, once per block per item
             const int ms = mit & 1;
             if (!mbar_wait_hint(m_empty + ms, ((mit >> 1) & 1) ^ 1, &g_err, 17, a.wait_ns)) { ok = false; break; }
             mbar_arrive_expect_tx(m_full + ms, kMSlotBytes);
@@ -314,7 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sC + (size_t)s * kCStageBytes, &cmap, kb * kCodeBytes, n0, ld_full + s);
           ++issued;
           if (++s == S) { s = 0; ph ^= 1; }
-          if (++mk == spm) mk = 0;
         }
       }
       {
@@ -339,11 +414,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       bool ok = true;
       int t_local = 0;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t_local) {
+      ItemIter it = items_begin(a, ntiles);
+      Item x;
+      while (ok && items_next(a, it, x)) {
         if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12, a.wait_ns)) { ok = false; break; }
         tc_fence_after();
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13, a.wait_ns) || !mbar_wait_hint(a_full + s, ph, &g_err, 13, a.wait_ns)) {
+        for (int kb = x.k0; kb < x.k1; ++kb) {
+          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13, a.wait_ns) ||
+              !mbar_wait_hint(a_full + s, ph, &g_err, 13, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -353,73 +431,136 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t at = tmem + BT + s * kAStageCols;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)   // K=16: 8 TMEM columns of A, +32 bytes of B (+2 in the address field)
-            umma_f16_ts(tmem, at + 8 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            umma_f16_ts(tmem, at + 8 * k, bd + 2 * k, idesc, (kb != x.k0 || k != 0) ? 1u : 0u);
           umma_commit(empty + s);
           if (++s == S) { s = 0; ph ^= 1; }
         }
         if (ok) umma_commit(tfull);
+        ++t_local;
       }
-      // every MMA issued (also those of a tile abandoned after a timeout) has
-      // finished before the TMEM is freed
+      // every MMA issued (also those of an item abandoned after a timeout)
+      // has finished before the TMEM is freed
       umma_commit(mma_drain);
       mbar_wait_hint(mma_drain, 0, nullptr, 0, a.wait_ns);
     }
   } else if (warp < kFirstDqWarp) {
     // ---------------- epilogue ----------------
     const int quad = warp & 3;                      // TMEM lanes this warp may read
+    const int r = quad * 32 + lane;                 // this thread's row of the tile
     int t_local = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_local) {
-      const int64_t m0 = (int64_t)(tile % a.tblocks) * BT;
-      const int64_t n = (int64_t)(tile / a.tblocks) * kBW + quad * 32 + lane;   // this thread's weight row
-      if (!mbar_wait_hint(tfull, t_local & 1, &g_err, 14, a.wait_ns)) break;
+    ItemIter it = items_begin(a, ntiles);
+    Item x;
+    while (items_next(a, it, x)) {
+      const int64_t m0 = (int64_t)(x.tile % a.tblocks) * BT;
+      const int wb = x.tile / a.tblocks;
+      const int64_t n = (int64_t)wb * kBW + r;      // this thread's weight row
+      // every epilogue thread takes the same branch (the split path below syncs them)
+      if (!named_bar_and(3, kEpiWarps * 32, mbar_wait_hint(tfull, t_local & 1, &g_err, 14, a.wait_ns))) break;
+      ++t_local;
       tc_fence_after();
       const bool nvalid = n < q.rows;
+      const bool whole = x.k0 == 0 && x.k1 == a.kblocks;
+      const int jn_all = a.M - m0 < BT ? (int)(a.M - m0) : BT;
+      float* pp = a.partials + ((size_t)blockIdx.x * 2 + x.slot) * (BT * kBW);
       const float bias = (a.bias && nvalid) ? load_f(a.bias, a.bias_dtype, n) : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c * 32, v);
-        if (c == BT / 32 - 1) {
-          // accumulator fully read: the MMA may start the next tile
+      for (int c = 0; c < BT / kCW; ++c) {
+        float v[kCW];
+        if constexpr (kCW == 32)
+          tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c * kCW, v);
+        else
+          tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + c * kCW, v);
+        if (c == BT / kCW - 1) {
+          // accumulator fully read: the MMA may start the next item
           tc_fence_before();
           mbar_arrive(tempty);
         }
+        if (!whole) {
+          // partial sums, [row][token]: each thread's row is contiguous, so
+          // both these stores and the final reduction's loads are 16 bytes wide
+          float4* dst = reinterpret_cast<float4*>(pp + (size_t)r * BT + c * kCW);
+#pragma unroll
+          for (int j = 0; j < kCW / 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          continue;
+        }
         if (!nvalid) continue;
-        const int64_t mb = m0 + c * 32;
-        const int jn = a.M - mb < 32 ? (int)(a.M - mb) : 32;
+        const int64_t mb = m0 + c * kCW;
+        const int jn = a.M - mb < kCW ? (int)(a.M - mb) : kCW;
         if (a.out_dtype == TS_F32) {
           float* op = reinterpret_cast<float*>(a.out) + mb * a.out_stride + n;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
+          for (int j = 0; j < kCW; ++j)
             if (j < jn) op[j * a.out_stride] = v[j] + bias;
         } else if (a.out_dtype == TS_BF16) {
           __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + mb * a.out_stride + n;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
+          for (int j = 0; j < kCW; ++j)
             if (j < jn) op[j * a.out_stride] = __float2bfloat16_rn(v[j] + bias);
         } else {
           __half* op = reinterpret_cast<__half*>(a.out) + mb * a.out_stride + n;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
+          for (int j = 0; j < kCW; ++j)
             if (j < jn) op[j * a.out_stride] = __float2half_rn(v[j] + bias);
         }
+      }
+      if (whole) continue;
+      // ---- split tile: the last CTA to arrive adds the pieces and stores ----
+      __threadfence();
+      named_bar_sync(3, kEpiWarps * 32);
+      if (r == 0) *epi_flag = atomicAdd(a.counters + x.tile, 1);
+      named_bar_sync(3, kEpiWarps * 32);
+      const int U = ntiles * a.kblocks;
+      const int G = gridDim.x;
+      const int u_lo = x.tile * a.kblocks, u_hi = u_lo + a.kblocks - 1;
+      const int c_first = (int)(((int64_t)(u_lo + 1) * G - 1) / U);   // CTA holding unit u_lo
+      const int c_last = (int)(((int64_t)(u_hi + 1) * G - 1) / U);
+      const int old = *epi_flag;
+      named_bar_sync(3, kEpiWarps * 32);                                // epi_flag is reused
+      if (old != c_last - c_first) continue;
+      __threadfence();
+      if (r == 0) a.counters[x.tile] = 0;
+      if (!nvalid) continue;
+      // 16 tokens at a time: four independent 16-byte loads per piece in
+      // flight, pieces added in CTA order
+      constexpr int kRT = BT < 16 ? BT : 16;
+      for (int j0 = 0; j0 < jn_all; j0 += kRT) {
+        float acc[kRT];
+#pragma unroll
+        for (int u = 0; u < kRT; ++u) acc[u] = 0.f;
+        for (int c = c_first; c <= c_last; ++c) {
+          const int slot = split_unit_begin(U, c, G) / a.kblocks == x.tile ? 0 : 1;
+          const float4* src = reinterpret_cast<const float4*>(
+              a.partials + ((size_t)c * 2 + slot) * (BT * kBW) + (size_t)r * BT + j0);
+          float4 t[kRT / 4];
+#pragma unroll
+          for (int u = 0; u < kRT / 4; ++u) t[u] = __ldcg(src + u);
+#pragma unroll
+          for (int u = 0; u < kRT / 4; ++u) {
+            acc[4 * u] += t[u].x;
+            acc[4 * u + 1] += t[u].y;
+            acc[4 * u + 2] += t[u].z;
+            acc[4 * u + 3] += t[u].w;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kRT; ++u)
+          if (j0 + u < jn_all) store_f(a.out, a.out_dtype, (m0 + j0 + u) * a.out_stride + n, acc[u] + bias);
       }
     }
   } else {
     // ---------------- dequantizers ----------------
     const int quad = warp & 3;
     const int half = ((warp - kFirstDqWarp) >> 2) & 1;   // columns [32 half, 32 half + 32) of a stage
-    const int grp = (warp - kFirstDqWarp) / kDqGroupWarps; // this group converts stages with kb % 2 == grp
+    const int grp = (warp - kFirstDqWarp) / kDqGroupWarps; // this group converts the item's stages j = grp, grp+2, ...
     const int rl = quad * 32 + lane;                      // tile row of this thread = TMEM lane
     const int gs = q.group_size;
     const bool dq = q.dqs_codes != nullptr;
     const int gph = gs >= 32 ? 1 : 32 / gs;               // groups in this thread's 32 columns (1 or 2)
     // Raw metadata of (row, group): 16-bit scale | 16-bit min << 16, or the
-    // two double-quant code bytes. From the TMA'd block in shared memory, or,
-    // when the metadata rows are not 16-byte multiples, loaded by this thread.
-    auto fetch = [&](int tile, int kb, uint32_t (&raw)[2]) {
-      const int64_t row = (int64_t)(tile / a.tblocks) * kBW + rl;
-      if (tile >= ntiles || row >= q.rows) return;
+    // two double-quant code bytes, loaded by this thread (metadata rows that
+    // are not 16-byte multiples).
+    auto fetch = [&](int64_t row, int kb, uint32_t (&raw)[2]) {
+      if (row >= q.rows) return;
       const int64_t flat = row * q.n_groups + ((kb * kBK + 32 * half) >> a.gs_shift);
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
@@ -450,28 +591,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    // Ring position of the tile's first stage (ts, tph), and the metadata
-    // block counter; each group walks only its own stages kb = grp, grp+2, ...
+    // Ring position of the item's first stage (ts, tph) and the metadata
+    // block counter (both groups wait for and release every block of an item)
     uint32_t mit = 0, tph = 0;
     int ts = 0;
     bool ok = true;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + BT + half * (kAStageCols / 2);
-    // Waits for the current metadata block and releases it without using it
-    // (a block that holds none of this group's stages).
-    auto pass_block = [&]() -> bool {
-      if (!mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18, a.wait_ns)) return false;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(m_empty + (mit & 1));
-      ++mit;
-      return true;
-    };
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const int64_t row = (int64_t)(tile / a.tblocks) * kBW + rl;
+    ItemIter it = items_begin(a, ntiles);
+    Item x;
+    while (ok && items_next(a, it, x)) {
+      const int64_t row = (int64_t)(x.tile / a.tblocks) * kBW + rl;
       const bool valid = row < q.rows;
       const int64_t row_ng = row * q.n_groups;
-      // Outliers of this row. Column-sorted rows use a cursor whose next
-      // (column, delta) is loaded right after the previous patch, so it has
-      // landed by the stage that needs it; other rows scan their list.
+      const int my_par = (x.k0 + grp) & 1;                // parity of the stages this group converts
+      // Outliers of this row inside the item's columns. Column-sorted rows use
+      // a cursor whose next (column, delta) is loaded right after the previous
+      // patch; other rows scan their table.
       int o_beg = 0, o_end = 0;
       bool sorted = true;
       if (valid && q.n_outliers > 0) {
@@ -480,8 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = o_beg + 1; j < o_end; ++j)
           if (q.ocol[j] < q.ocol[j - 1]) { sorted = false; break; }
       }
-      // the cursor skips outliers in the other thread's half and the other
-      // group's stages
+      const int col_lo = x.k0 * kBK, col_hi = x.k1 * kBK;
       int cur = o_beg;
       int next_col = INT_MAX;
       float next_delta = 0.f;
@@ -489,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         next_col = INT_MAX;
         while (cur < o_end) {
           const int c = q.ocol[cur];
-          if (((c >> 5) & 1) == half && ((c >> 6) & 1) == grp) {
+          if (c >= col_lo && c < col_hi && ((c >> 5) & 1) == half && ((c >> 6) & 1) == my_par) {
             next_col = c;
             next_delta = __half2float(q.odelta[cur]);
             break;
@@ -499,109 +633,104 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       if (sorted) advance();
 
-      // ring position of this group's first stage in the tile
-      int s = ts + grp;
-      uint32_t ph = tph;
-      while (s >= S) { s -= S; ph ^= 1; }
-      if (a.meta_tma && grp >= KB && !pass_block()) { ok = false; break; }   // no stage of ours in the tile
-      for (int kb = grp; kb < KB; kb += kDqGroups) {
-        const int cs = s;
-        const uint32_t cph = ph;
-        s += kDqGroups;
-        while (s >= S) { s -= S; ph ^= 1; }
-        const int cmk = kb % spm;                           // stage within its metadata block
-        const int c0 = kb * kBK + 32 * half;               // first column of this thread's half
-        uint32_t rawc[2] = {0, 0};
-        if (a.meta_tma) {
-          // Both groups wait for every metadata block and release it after
-          // their last stage in it, so a release can never be counted toward
-          // an older use of the slot.
-          if (cmk < kDqGroups &&
-              !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18, a.wait_ns)) { ok = false; break; }
-          const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
-          const int ib = ((cmk << 6) + 32 * half) >> a.gs_shift;   // group of c0 within the block
-#pragma unroll
-          for (int gi = 0; gi < 2; ++gi) {
-            if (gi < gph) {
-              if (dq)
-                rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[kBW * 16 + ib + gi] << 8);
-              else
-                rawc[gi] = (uint32_t)reinterpret_cast<const uint16_t*>(slot)[ib + gi] |
-                           ((uint32_t)reinterpret_cast<const uint16_t*>(slot + kBW * 16)[ib + gi] << 16);
-            }
-          }
-          if (cmk + kDqGroups >= spm || kb + kDqGroups >= KB) {
-            // one arrival per warp: 256 arrivals on one barrier word would
-            // serialize in the shared-memory atomic unit every stage
-            __syncwarp();
-            if (lane == 0) mbar_arrive(m_empty + (mit & 1));
-            ++mit;
-            // a one-stage tail block owned by the other group
-            if (kb + kDqGroups >= KB && kb + 1 < KB && (kb + 1) % spm == 0 && !pass_block()) {
-              ok = false;
-              break;
-            }
-          }
-        } else {
-          fetch(tile, kb, rawc);
+      const int nst = x.k1 - x.k0;
+      for (int b = x.k0 / spm; ok && b * spm < x.k1; ++b) {
+        const int kb_lo = max(x.k0, b * spm), kb_hi = min(x.k1, (b + 1) * spm);
+        if (a.meta_tma && !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18, a.wait_ns)) {
+          ok = false;
+          break;
         }
-        float2 sg[2];
-        if (valid) decode(row_ng, kb, rawc, sg);
-
-        if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15, a.wait_ns) ||
-            !mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
-        const unsigned char* crow = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes + half * (kCodeBytes / 2);
-        uint32_t cw[kCodeBytes / 8];
-        if (kCodeBytes / 2 >= 16) {
+        const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
+        // first stage of this group in the block: local index j = kb - k0 with j % 2 == grp
+        int kb = kb_lo + (((kb_lo - x.k0) & 1) != grp ? 1 : 0);
+        for (; kb < kb_hi; kb += kDqGroups) {
+          const int j = kb - x.k0;
+          const int sp = ts + j;
+          const int cs = sp % S;
+          const uint32_t cph = tph ^ (uint32_t)((sp / S) & 1);
+          const int c0 = kb * kBK + 32 * half;                // first column of this thread's half
+          uint32_t rawc[2] = {0, 0};
+          if (a.meta_tma) {
+            const int ib = (((kb % spm) << 6) + 32 * half) >> a.gs_shift;   // group of c0 within the block
 #pragma unroll
-          for (int i2 = 0; i2 < kCodeBytes / 32; ++i2) {
-            const uint4 u = reinterpret_cast<const uint4*>(crow)[i2];
-            cw[4 * i2] = u.x; cw[4 * i2 + 1] = u.y; cw[4 * i2 + 2] = u.z; cw[4 * i2 + 3] = u.w;
-          }
-        } else {
-          const uint2 u = *reinterpret_cast<const uint2*>(crow);
-          cw[0] = u.x; cw[kCodeBytes / 8 - 1] = u.y;
-        }
-        uint32_t wv[16];
-        if (!valid) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) wv[j] = 0;
-        } else if (gph == 1) {
-          convert_half<BITS, CB, XT, 1>(cw, sg, cbs, wv);
-        } else {
-          convert_half<BITS, CB, XT, 2>(cw, sg, cbs, wv);
-        }
-        // outliers in this thread's 32 columns: value = fp32(base) + delta, rounded once
-        if (valid && o_end > o_beg) {
-          if (sorted) {
-            while (next_col < c0 + 32) {
-              const int cc = next_col - c0;
-              const uint32_t byte = crow[cc * BITS / 8];
-              const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
-              const float2 g = (gph == 2 && cc >= 16) ? sg[1] : sg[0];
-              const float v = CB ? cbs[code] : (float)code;
-              const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
-              patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
-              ++cur;
-              advance();
+            for (int gi = 0; gi < 2; ++gi) {
+              if (gi < gph) {
+                if (dq)
+                  rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[kBW * 16 + ib + gi] << 8);
+                else
+                  rawc[gi] = (uint32_t)reinterpret_cast<const uint16_t*>(slot)[ib + gi] |
+                             ((uint32_t)reinterpret_cast<const uint16_t*>(slot + kBW * 16)[ib + gi] << 16);
+              }
             }
           } else {
-            for (int j = o_beg; j < o_end; ++j) {
-              const int c = q.ocol[j];
-              if (c < c0 || c >= c0 + 32) continue;
-              const float val = outlier_value<CB>(q, cbs, row, c, j);
-              patch_half(wv, c - c0, pack2<XT>(val, val) & 0xFFFFu);
+            fetch(row, kb, rawc);
+          }
+          float2 sg[2];
+          if (valid) decode(row_ng, kb, rawc, sg);
+
+          if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15, a.wait_ns) ||
+              !mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
+          const unsigned char* crow = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes + half * (kCodeBytes / 2);
+          uint32_t cw[kCodeBytes / 8];
+          if (kCodeBytes / 2 >= 16) {
+#pragma unroll
+            for (int i2 = 0; i2 < kCodeBytes / 32; ++i2) {
+              const uint4 u = reinterpret_cast<const uint4*>(crow)[i2];
+              cw[4 * i2] = u.x; cw[4 * i2 + 1] = u.y; cw[4 * i2 + 2] = u.z; cw[4 * i2 + 3] = u.w;
+            }
+          } else {
+            const uint2 u = *reinterpret_cast<const uint2*>(crow);
+            cw[0] = u.x; cw[kCodeBytes / 8 - 1] = u.y;
+          }
+          uint32_t wv[16];
+          if (!valid) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) wv[jj] = 0;
+          } else if (gph == 1) {
+            convert_half<BITS, CB, XT, 1>(cw, sg, cbs, wv);
+          } else {
+            convert_half<BITS, CB, XT, 2>(cw, sg, cbs, wv);
+          }
+          // outliers in this thread's 32 columns: value = fp32(base) + delta, rounded once
+          if (valid && o_end > o_beg) {
+            if (sorted) {
+              while (next_col < c0 + 32) {
+                const int cc = next_col - c0;
+                const uint32_t byte = crow[cc * BITS / 8];
+                const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
+                const float2 g = (gph == 2 && cc >= 16) ? sg[1] : sg[0];
+                const float v = CB ? cbs[code] : (float)code;
+                const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
+                patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
+                ++cur;
+                advance();
+              }
+            } else {
+              for (int jo = o_beg; jo < o_end; ++jo) {
+                const int c = q.ocol[jo];
+                if (c < c0 || c >= c0 + 32) continue;
+                const float val = outlier_value<CB>(q, cbs, row, c, jo);
+                patch_half(wv, c - c0, pack2<XT>(val, val) & 0xFFFFu);
+              }
             }
           }
+          tmem_st16(lane_base + cs * kAStageCols, wv);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(a_full + cs);
         }
-        tmem_st16(lane_base + cs * kAStageCols, wv);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(a_full + cs);
+        if (!ok) break;
+        if (a.meta_tma) {
+          // one arrival per warp: 256 arrivals on one barrier word would
+          // serialize in the shared-memory atomic unit every block
+          __syncwarp();
+          if (lane == 0) mbar_arrive(m_empty + (mit & 1));
+          ++mit;
+        }
       }
-      // the next tile starts KB stages later in the ring
-      const int adv = ts + KB;
+      // the next item starts nst stages later in the ring
+      const int adv = ts + nst;
       const int wraps = adv / S;
       ts = adv - wraps * S;
       tph ^= (uint32_t)(wraps & 1);
@@ -622,13 +751,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 static size_t qgemm_smem(int BT, int bits, int S) {
   const size_t stage = (size_t)BT * qgemm::kBK * 2 + (size_t)qgemm::kBW * qgemm::kBK * bits / 8;
-  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 9) * 8 + 16 + 256 * 4;
+  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 9) * 8 + 16 + 256 * 4 + 16;
 }
 
 static int max_stages(int BT) { return (qgemm::kTmemCols - BT) / qgemm::kAStageCols; }
 
 // Layout conditions of the tensor-core path (everything else uses the GEMV).
-bool qgemm_supported(const ts_qweight& w, const void* x, int64_t x_stride) {
+static bool qgemm_layout_ok(const ts_qweight& w) {
   if (!(w.bits == 2 || w.bits == 4 || w.bits == 8)) return false;
   const int gs = w.group_size;
   if (gs < 16 || (gs & (gs - 1)) != 0) return false;   // power-of-two groups of at least 16
@@ -636,16 +765,71 @@ bool qgemm_supported(const ts_qweight& w, const void* x, int64_t x_stride) {
   if (kb * qgemm::kBK > w.padded_cols || kb * qgemm::kBK * w.bits / 8 > w.packed_row_bytes) return false;
   if (w.packed_row_bytes % 16 != 0 || !is_aligned(w.packed, 16)) return false;
   if (w.rows * w.n_groups >= (int64_t(1) << 31) || w.rows >= (int64_t(1) << 31)) return false;
-  if (!is_aligned(x, 16) || (x_stride * 2) % 16 != 0) return false;
   if (w.cols < 1) return false;
   return max_smem_optin() >= (int)qgemm_smem(256, w.bits, 2);
+}
+
+bool qgemm_supported(const ts_qweight& w, const void* x, int64_t x_stride) {
+  return qgemm_layout_ok(w) && is_aligned(x, 16) && (x_stride * 2) % 16 == 0;
+}
+
+// Tile plan for M tokens: BT tokens per tile (16/32/64 for decode-sized M,
+// 128/256 for prefill), and whether CTAs split tiles along K.
+struct QgemmPlan {
+  int BT, tblocks, wblocks, kblocks, ntiles, grid;
+  bool split_wanted;
+};
+
+static QgemmPlan qgemm_plan(const ts_qweight& w, int64_t M) {
+  QgemmPlan p;
+  const int sms = sm_count();
+  p.wblocks = (int)((w.rows + qgemm::kBW - 1) / qgemm::kBW);
+  p.kblocks = (int)((w.cols + qgemm::kBK - 1) / qgemm::kBK);
+  if (M <= 16) p.BT = 16;
+  else if (M <= 32) p.BT = 32;
+  else if (M <= 64) p.BT = 64;
+  else if ((int64_t)((M + 255) / 256) * p.wblocks < sms) p.BT = 128;   // 256 would leave SMs idle
+  else p.BT = 256;   // 256-token tiles halve the dequantization per flop
+  p.tblocks = (int)((M + p.BT - 1) / p.BT);
+  p.ntiles = p.tblocks * p.wblocks;
+  // decode-sized M: the few tiles' K-stages are split evenly over the SMs.
+  // Prefill keeps whole tiles per CTA: measured, split plans were 4-20%
+  // slower there (partial sums and their reduction cost more than the wave
+  // imbalance they remove).
+  p.split_wanted = p.BT <= 64;
+  const int64_t units = (int64_t)p.ntiles * p.kblocks;
+  p.grid = (int)std::min<int64_t>(p.split_wanted ? units : p.ntiles, sms);
+  return p;
+}
+
+static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+static size_t qgemm_partials_bytes(int grid, int BT) { return align256((size_t)grid * 2 * BT * qgemm::kBW * 4); }
+
+// Extra workspace the split plan needs beyond the decode kernel's: its tile
+// counters share the zeroed counter area after the error flag, and its
+// partial sums sit at the end of the workspace (never over a counter area).
+size_t qgemm_workspace_extra(const ts_qweight& w, int64_t M, size_t counters_bytes_gemv) {
+  if (!qgemm_layout_ok(w) || M < 1) return 0;
+  const QgemmPlan p = qgemm_plan(w, M);
+  if (!p.split_wanted) return 0;
+  const size_t cnt = align256((size_t)p.ntiles * 4);
+  return (cnt > counters_bytes_gemv ? cnt - counters_bytes_gemv : 0) + qgemm_partials_bytes(p.grid, p.BT);
 }
 
 template <int BITS, bool CB, int XT, int BT>
 static int launch_qgemm(const CUtensorMap* maps, const qgemm::Args& a, int grid, size_t smem, cudaStream_t st) {
   auto k = qgemm::qgemm_kernel<BITS, CB, XT, BT>;
-  TS_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<grid, qgemm::kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
+  static thread_local int configured_dev = -1;
+  static thread_local size_t configured_smem = 0;
+  int dev = 0;
+  TS_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_dev != dev || configured_smem < smem) {
+    TS_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured_dev = dev;
+    configured_smem = smem;
+  }
+  k<<<grid, qgemm::kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4], a);
   TS_LAUNCH_CHECK();
   return TS_OK;
 }
@@ -653,8 +837,13 @@ static int launch_qgemm(const CUtensorMap* maps, const qgemm::Args& a, int grid,
 template <int BITS, bool CB, int XT>
 static int launch_bt(int BT, const CUtensorMap* maps, const qgemm::Args& a, int grid, size_t smem,
                      cudaStream_t st) {
-  if (BT == 256) return launch_qgemm<BITS, CB, XT, 256>(maps, a, grid, smem, st);
-  return launch_qgemm<BITS, CB, XT, 128>(maps, a, grid, smem, st);
+  switch (BT) {
+    case 16: return launch_qgemm<BITS, CB, XT, 16>(maps, a, grid, smem, st);
+    case 32: return launch_qgemm<BITS, CB, XT, 32>(maps, a, grid, smem, st);
+    case 64: return launch_qgemm<BITS, CB, XT, 64>(maps, a, grid, smem, st);
+    case 128: return launch_qgemm<BITS, CB, XT, 128>(maps, a, grid, smem, st);
+    default: return launch_qgemm<BITS, CB, XT, 256>(maps, a, grid, smem, st);
+  }
 }
 
 template <int BITS>
@@ -667,9 +856,28 @@ static int launch_bits(bool cb, int xt, int BT, const CUtensorMap* maps, const q
             : launch_bt<BITS, false, 0>(BT, maps, a, grid, smem, st);
 }
 
+// Whether a call of M tokens runs split with this workspace: the counters
+// (from `counters_off`) and the partial sums (at the end) must both fit.
+bool qgemm_split_fits(const ts_qweight& w, int64_t M, size_t counters_off, size_t ws_bytes) {
+  if (!qgemm_layout_ok(w)) return false;
+  const QgemmPlan p = qgemm_plan(w, M);
+  if (!p.split_wanted) return false;
+  const size_t need = counters_off + align256((size_t)p.ntiles * 4) + qgemm_partials_bytes(p.grid, p.BT);
+  return ws_bytes >= need;
+}
+
+// The tensor-core path. With `workspace` (counters zeroed from counters_off,
+// partial sums at the end) a plan that wants split runs split; without, whole
+// tiles per CTA (decode-sized M then needs the workspace: the caller routes
+// those calls to the GEMV instead).
 int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride, const void* bias,
-              int bias_dtype, void* out, int out_dtype, int64_t out_stride, cudaStream_t stream) {
+              int bias_dtype, void* out, int out_dtype, int64_t out_stride, void* workspace, size_t counters_off,
+              size_t ws_bytes, cudaStream_t stream) {
   TS_UNSUPPORTED(qgemm_supported(w, x, x_stride), "qgemm: layout not supported");
+  QgemmPlan p = qgemm_plan(w, M);
+  const bool split = p.split_wanted && workspace != nullptr && qgemm_split_fits(w, M, counters_off, ws_bytes);
+  const int sms = sm_count();
+  if (!split) p.grid = (int)std::min<int64_t>(p.ntiles, sms);
   qgemm::Args a;
   a.q = make_qw(w);
   a.M = M;
@@ -678,21 +886,21 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   a.out = out;
   a.out_dtype = out_dtype;
   a.out_stride = out_stride;
-  a.wblocks = (int)((w.rows + qgemm::kBW - 1) / qgemm::kBW);
-  a.kblocks = (int)((w.cols + qgemm::kBK - 1) / qgemm::kBK);
-  const int sms = sm_count();
-  // 256-token tiles halve the dequantization per flop; 128-token tiles when
-  // 256 would leave SMs idle
-  int BT = 256;
-  if ((int64_t)((M + 255) / 256) * a.wblocks < sms) BT = 128;
-  a.tblocks = (int)((M + BT - 1) / BT);
+  a.wblocks = p.wblocks;
+  a.kblocks = p.kblocks;
+  a.tblocks = p.tblocks;
+  a.split = split ? 1 : 0;
+  a.counters = split ? reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + counters_off) : nullptr;
+  a.partials = split ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ws_bytes -
+                                                qgemm_partials_bytes(p.grid, p.BT))
+                     : nullptr;
+  const int BT = p.BT;
   int S = max_stages(BT);
   while (S > 2 && qgemm_smem(BT, w.bits, S) > (size_t)max_smem_optin()) --S;
   a.stages = S;
   const size_t smem = qgemm_smem(BT, w.bits, S);
-  const int64_t ntiles = (int64_t)a.tblocks * a.wblocks;
-  const int grid = (int)std::min<int64_t>(ntiles, sms);
-  CUtensorMap maps[4];
+  const int grid = p.grid;
+  CUtensorMap maps[5];
   int rc = encode_tmap_2d(&maps[0], x, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)w.cols, (uint64_t)M,
                           (uint64_t)x_stride * 2, qgemm::kBK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TS_OK) return rc;
@@ -700,6 +908,14 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
                       (uint64_t)w.rows, (uint64_t)w.packed_row_bytes, qgemm::kBK * w.bits / 8, qgemm::kBW,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc != TS_OK) return rc;
+  // the same codes with 256-byte-wide boxes, for the L2 prefetch
+  a.prefetch_codes = w.packed_row_bytes >= 256 ? 1 : 0;
+  maps[4] = maps[1];
+  if (a.prefetch_codes) {
+    rc = encode_tmap_2d(&maps[4], w.packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)w.packed_row_bytes,
+                        (uint64_t)w.rows, (uint64_t)w.packed_row_bytes, 256, qgemm::kBW, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TS_OK) return rc;
+  }
   // group metadata blocks of 16 bytes per row: 8 fp16 scales/mins, or 16
   // double-quant code bytes; rows must be 16-byte multiples for the copies
   const bool dq = w.dq_scale_codes != nullptr;
@@ -754,5 +970,6 @@ int qgemm_error_flag(int* code, bool clear, cudaStream_t stream) {
   *code = v;
   return TS_OK;
 }
+
 
 }  // namespace ts

@@ -95,9 +95,9 @@ def test_config4_forced_bits(shape, bits):
     assert not esc
     q = goap.quantize(w_np, bits=bits, group_size=128, outlier_frac=0.001, mode="uniform")
     assert_device_quant_equals_oracle(d, q)
-    w32 = w_np.astype(np.float32)
-    ref_err = np.linalg.norm(w32 - goap.dequantize(q)) / np.linalg.norm(w32)
-    assert abs(err - ref_err) <= 1e-5 * ref_err
+    w64 = w_np.astype(np.float64)
+    ref_err = np.linalg.norm(w64 - goap.dequantize(q)) / np.linalg.norm(w64)
+    assert abs(err - ref_err) <= 1e-4 * ref_err   # the device sums fp32 squares
     _check_gemm(ts.QuantLinear.from_device_quant(d), q, (1, 16, 128))
 
 
@@ -116,11 +116,11 @@ def test_adaptive_escalation_matches_oracle():
     relative Frobenius error is within the threshold, the last one always."""
     import tensorshrink_b200 as ts
     w_np = goap.student_t_weights((1024, 2048), seed=99)
-    w32 = w_np.astype(np.float32)
+    w64 = w_np.astype(np.float64)
     errs = {}
     for b in (2, 4, 8):
         q = goap.quantize(w_np, bits=b, group_size=128, outlier_frac=0.001, mode="uniform")
-        errs[b] = np.linalg.norm(w32 - goap.dequantize(q)) / np.linalg.norm(w32)
+        errs[b] = np.linalg.norm(w64 - goap.dequantize(q)) / np.linalg.norm(w64)
     assert errs[2] > errs[4] > errs[8]
     w = torch.from_numpy(w_np).cuda()
     cases = [(0.5 * (errs[2] + errs[4]), 4, True),      # 2-bit too coarse, 4-bit accepted
@@ -130,7 +130,7 @@ def test_adaptive_escalation_matches_oracle():
         qt, err, esc = ts.quantize_tensor_adaptive(w, group_size=128, outlier_frac=0.001,
                                                    error_threshold=thr, allowed_bits=(2, 4, 8))
         assert (qt.bits, esc) == (want_bits, want_esc), thr
-        assert abs(err - errs[want_bits]) <= 1e-5 * errs[want_bits]
+        assert abs(err - errs[want_bits]) <= 1e-4 * errs[want_bits]
         q = goap.quantize(w_np, bits=want_bits, group_size=128, outlier_frac=0.001, mode="uniform")
         np.testing.assert_array_equal(qt.packed, q.packed)
         np.testing.assert_array_equal(qt.outlier_idx, q.outlier_idx)

@@ -126,3 +126,61 @@ def test_two_nccl_ranks():
     for rank, errs, err in res:
         assert err is None, (rank, err)
         assert max(errs) <= TOL, (rank, errs)
+
+
+def _decoder_worker(rank, world, port, q):
+    """Each rank builds the tensor-parallel decoder (whole layers quantized
+    identically everywhere, then cut) and an unsharded copy in a one-rank
+    group; the last-position logits after a prefill, and the tokens of a few
+    decode steps, must agree."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+        from tensorshrink_b200.decoder import DecoderConfig, QuantDecoder
+        solo = [dist.new_group([r]) for r in range(world)][rank]
+        cfg = DecoderConfig(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=4, intermediate=2048, vocab=4000,
+                            layer_bits=[4, 8], seed=11)
+        tp_model = QuantDecoder(cfg, "cuda", max_batch=2, max_seq=64)
+        ref_model = QuantDecoder(cfg, "cuda", group=solo, max_batch=2, max_seq=64)
+        g = torch.Generator(device="cuda").manual_seed(4)
+        tokens = torch.randint(0, cfg.vocab, (2, 10), device="cuda", generator=g)
+        a = tp_model.prefill(tokens, return_logits=True)
+        b = ref_model.prefill(tokens, return_logits=True)
+        err = ((a - b).abs().max() / b.abs().max()).item()
+        cur_a = a.argmax(-1)
+        cur_b = b.argmax(-1)
+        agree, total = int((cur_a == cur_b).sum()), 2
+        for step in range(4):
+            pos = torch.tensor([10 + step], device="cuda")
+            cur_a = tp_model.decode_step(cur_b, pos)
+            nb = ref_model.decode_step(cur_b, pos)
+            agree += int((cur_a == nb).sum())
+            total += 2
+            cur_b = nb
+        q.put((rank, [err, 1.0 - agree / total], None))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_decoder(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decoder_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, vals, err in res:
+        assert err is None, (rank, err)
+        logit_err, disagree = vals
+        assert logit_err <= 2e-2, (rank, logit_err)
+        assert disagree <= 0.25, (rank, disagree)

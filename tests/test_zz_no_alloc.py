@@ -56,16 +56,19 @@ def _noalloc(lib, qw, x, out, bias=None):
     (512, 1024, 8, "uniform", True, 16),
 ])
 def test_noalloc_matches_workspace_entry(lib, rows, cols, bits, mode, dq, M):
-    """Bit-identical to ts_qlinear (same kernel, same partition, only the
-    scratch differs) on two calls in a row, and within the parity tolerance
+    """Bit-identical to ts_qlinear given a caller workspace of the same size
+    as the fixed array (same kernel, same partition, only the scratch's
+    owner differs) on two calls in a row, and within the parity tolerance
     of the oracle's fp32 dequant-matmul."""
     from tensorshrink_b200 import kernels
     ql = _layer(rows, cols, bits, mode, dq, seed=rows + cols + bits)
     qw = ql.qweight()
-    assert lib.ts_qlinear_workspace_size(C.byref(qw), M) <= lib.ts_qlinear_noalloc_max_scratch()
+    limit = int(lib.ts_qlinear_noalloc_max_scratch())
+    assert lib.ts_qlinear_workspace_size(C.byref(qw), 1) <= limit
     x = torch.randn(M, cols, device="cuda").to(torch.bfloat16)
     bias = torch.randn(rows, device="cuda").to(torch.bfloat16) * 0.1
-    ref = kernels.qlinear(x, qw, bias, torch.float32)
+    ws = torch.zeros(limit, dtype=torch.uint8, device="cuda")
+    ref = kernels.qlinear(x, qw, bias, torch.float32, workspace=ws)
     W = goap.dequantize(ql.to_quantized_tensor())
     y_oracle = x.float().cpu().numpy() @ W.T + bias.float().cpu().numpy()
     for _ in range(2):
