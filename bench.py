@@ -158,7 +158,10 @@ def layer_of(p):
     return getattr(p, "local", p)
 
 
-def mlp_step(blocks, x, world=1):
+def mlp_step(blocks, x, world=1, exchange=None):
+    """One decode step through the MLP blocks. With world > 1 the down
+    projection's fp32 partial sums are summed over the ranks by the
+    library's one-shot NVLink all-reduce (`exchange`), or NCCL without one."""
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
@@ -168,7 +171,10 @@ def mlp_step(blocks, x, world=1):
             x = down(m)
         else:
             y = down(m, torch.float32)          # this rank's partial sum
-            dist.all_reduce(y)
+            if exchange is not None:
+                y = exchange.all_reduce(y, out=y)
+            else:
+                dist.all_reduce(y)
             x = y.to(torch.bfloat16)
     return x
 
@@ -368,7 +374,41 @@ def decode_sweep(device, blocks, reps=50):
     return res
 
 
-def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32):
+def quantize_all_layers_measure(device, n_layers=80):
+    """BASELINE config 5 (i): GPU quantize+pack of every projection of 80
+    Llama-70B-shaped layers (68.45 B weights, 4-bit g128 double-quant NF4,
+    0.1% outliers). Each weight is drawn on the device (untimed), then
+    quantize_device runs between CUDA events; the sum over all 560 calls is
+    the measured time."""
+    import torch
+    import tensorshrink_b200 as ts
+    from tensorshrink_b200.decoder import llama_70b_config
+    cfg = llama_70b_config()
+    H, D, F_ = cfg.hidden, cfg.head_dim, cfg.intermediate
+    shapes = [(cfg.n_heads * D, H), (cfg.n_kv_heads * D, H), (cfg.n_kv_heads * D, H), (H, cfg.n_heads * D),
+              (F_, H), (F_, H), (H, F_)]
+    total_ms, elems, calls = 0.0, 0, 0
+    for layer in range(n_layers):
+        for j, shape in enumerate(shapes):
+            w = student_t_cuda(shape, 90000 + 16 * layer + j, device)
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            d = ts.quantize_device(w, bits=4, group_size=128, outlier_frac=0.001, double_quant=True, nf_quant=True)
+            e_ev.record()
+            e_ev.synchronize()
+            total_ms += s_ev.elapsed_time(e_ev)
+            elems += w.numel()
+            calls += 1
+            del w, d
+    return {"metric": "GPU quantize+pack of all Llama-70B-shaped weights", "layers": n_layers, "calls": calls,
+            "params": elems, "seconds": round(total_ms / 1e3, 3),
+            "fp16_input_GB/s": round(2 * elems / (total_ms * 1e-3) / 1e9, 1),
+            "config": "4-bit g128 double-quant NF4, 0.1% outliers; weights drawn per call on the device "
+                      "(not timed); CUDA events around each quantize_device call, summed"}
+
+
+def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32, cfg=None, prefill=True,
+                    exchange=None):
     """the Llama-3-8B-shaped decoder (32 layers, per-layer
     bits drawn from 2/4/8 with a fixed seed, g128 uniform + 0.1% outliers),
     tensor-parallel over the `world` ranks. Decode: B sequences with `ctx`
@@ -378,17 +418,21 @@ def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32
     import torch
     import torch.distributed as dist
     from tensorshrink_b200.decoder import CUDAGraphDecoder, QuantDecoder, llama3_8b_config
-    cfg = llama3_8b_config(seed=0)
-    model = QuantDecoder(cfg, device, max_batch=max(batches), max_seq=2048)
+    cfg = cfg or llama3_8b_config(seed=0)
+    model = QuantDecoder(cfg, device, exchange=exchange, max_batch=max(batches),
+                         max_seq=2048 if prefill else ctx + steps + 16)
     packed = float(model.packed_nbytes())
     if world > 1:
         t = torch.tensor([packed], device=device, dtype=torch.float64)
         dist.all_reduce(t)
         packed = float(t.item())
     g = torch.Generator(device=device).manual_seed(0)
-    res = {"workload": "llama3_8b_shaped_32L_bits_2_4_8_seeded_g128_uniform_outlier0.001",
+    res = {"workload": (f"llama_{cfg.n_layers}L_h{cfg.hidden}_i{cfg.intermediate}_bits_"
+                        f"{'_'.join(map(str, sorted(set(model.layer_bits))))}_g{cfg.group_size}"
+                        f"{'_dq' if cfg.double_quant else ''}{'_nf' if cfg.nf_quant else '_uniform'}_outlier0.001"),
            "layer_bits": model.layer_bits, "packed_bytes_all_ranks": int(packed),
-           "parallelism": f"tp x{world}" if world > 1 else "single GPU",
+           "parallelism": (f"tp x{world}, " + ("NCCL" if exchange is None else "one-shot NVLink all-reduce kernel"))
+                          if world > 1 else "single GPU",
            "attention": "plain torch SDPA over a static bf16 KV cache (outside the measured path)",
            "decode": []}
     attn_len = ctx + steps + 8
@@ -403,10 +447,11 @@ def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32
                               "tokens_per_s": round(B / (ms * 1e-3), 1),
                               "packed_GB/s": round(packed / (ms * 1e-3) / 1e9, 1)})
         del runner
-    tokens = torch.randint(0, cfg.vocab, (1, 2048), device=device, generator=g)
-    model.prefill(tokens)
-    ms = timed(lambda: model.prefill(tokens), 3) / 3
-    res["prefill_2048"] = {"ms": round(ms, 3), "tokens_per_s": round(2048 / (ms * 1e-3), 1)}
+    if prefill:
+        tokens = torch.randint(0, cfg.vocab, (1, 2048), device=device, generator=g)
+        model.prefill(tokens)
+        ms = timed(lambda: model.prefill(tokens), 3) / 3
+        res["prefill_2048"] = {"ms": round(ms, 3), "tokens_per_s": round(2048 / (ms * 1e-3), 1)}
     del model
     torch.cuda.empty_cache()
     return res
@@ -425,17 +470,21 @@ def run_ours(args, rank, world, device):
     hbm_peak, _, peak_kind = peaks()
     blocks = build_blocks(args.blocks, device, world=world, rank=rank)
     M = args.M
+    exchange = None
+    if world > 1 and not args.nccl:
+        from tensorshrink_b200.comm import PeerExchange
+        exchange = PeerExchange(max_floats=1 << 20, device=device)
     x0 = torch.randn(M, HIDDEN, device=device).to(torch.bfloat16)
     static_x = x0.clone()
 
     # ---- capture one step as a CUDA graph ----
     for _ in range(2):
-        mlp_step(blocks, static_x, world)
+        mlp_step(blocks, static_x, world, exchange)
     torch.cuda.synchronize(device)
     _C.launch_count(reset=True)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        static_y = mlp_step(blocks, static_x, world)
+        static_y = mlp_step(blocks, static_x, world, exchange)
     launches_per_step = _C.launch_count(reset=True)
 
     for _ in range(max(args.warmup, 3)):
@@ -514,7 +563,7 @@ def run_ours(args, rank, world, device):
 
     def e2e_step():
         xd.copy_(xh, non_blocking=True)
-        y = mlp_step(blocks, xd, world)
+        y = mlp_step(blocks, xd, world, exchange)
         yh.copy_(y, non_blocking=True)
 
     for _ in range(3):
@@ -550,7 +599,13 @@ def run_ours(args, rank, world, device):
         cpu = cpu_baseline(blocks, M, budget_s=args.cpu_seconds)
     del blocks, graph, kgraph, e2e_graph
     torch.cuda.empty_cache()
-    decoder = decoder_measure(device, world, timed) if not args.no_decoder else None
+    decoder = decoder_measure(device, world, timed, exchange=exchange) if not args.no_decoder else None
+    decoder70 = None
+    if not args.no_decoder:
+        from tensorshrink_b200.decoder import llama_70b_config
+        decoder70 = decoder_measure(device, world, timed, batches=(1, 32), cfg=llama_70b_config(), prefill=False,
+                                    exchange=exchange)
+    quant_all = quantize_all_layers_measure(device) if solo and not args.no_prefill else None
 
     out = None
     if rank == 0:
@@ -573,8 +628,9 @@ def run_ours(args, rank, world, device):
                 "bytes_per_step": bytes_step,
                 "l2": f"inputs larger than L2: {args.blocks} distinct MLP blocks "
                       f"({bytes_step / 1e6:.0f} MB packed) streamed per step",
-                "parallelism": f"tp x{world} (gate/up column-parallel, down row-parallel + NCCL all-reduce "
-                               f"of fp32 partials)" if world > 1 else "single GPU",
+                "parallelism": (f"tp x{world} (gate/up column-parallel, down row-parallel + "
+                                f"{'NCCL all-reduce' if exchange is None else 'one-shot NVLink all-reduce kernel'}"
+                                f" of fp32 partials)") if world > 1 else "single GPU",
                 "timing": "CUDA graph of one step, K replays between CUDA events, max over ranks",
             },
             "tokens_per_s": round(M / (ms_per_step * 1e-3), 1),
@@ -602,6 +658,8 @@ def run_ours(args, rank, world, device):
             "quantize": quant,
             "sweeps": sweeps,
             "decoder": decoder,
+            "decoder_70b": decoder70,
+            "quantize_all_70b": quant_all,
         }
     return out
 
@@ -705,6 +763,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-sweeps", action="store_true", help="skip the per-config M sweeps")
     ap.add_argument("--no-decoder", action="store_true", help="skip the Llama-3-8B-shaped decoder")
+    ap.add_argument("--nccl", action="store_true", help="tensor-parallel exchanges through NCCL instead of the "
+                                                       "library's one-shot all-reduce kernel")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()

@@ -164,6 +164,29 @@ TS_API int ts_outlier_tables_from_stream(const ts_qweight* w, const void* row_de
                                          int32_t* col_out, uint16_t* delta_out, int32_t* row_ptr_out,
                                          int* bad_flag, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * One-shot all-reduce over NVLink peer memory for tensor-parallel layers.
+ * Replaces, for the row-parallel partial sums, the torch.distributed
+ * all_reduce the reference's multi-GPU path would use (the reference itself
+ * has no tensor parallelism; its layers run on one device).
+ * Each rank allocates one exchange buffer (ts_peer_alloc, zeroed; bytes from
+ * ts_peer_buffer_bytes), shares its CUDA IPC handle (ts_ipc_get_handle, 64
+ * bytes) and maps the others (ts_ipc_open). ts_allreduce_oneshot then sums
+ * `n` floats of `in` over the ranks (rank order, identical on every rank)
+ * plus an optional `residual`, into `out` (which may alias either). Every
+ * rank must make the same sequence of calls with the same n; n <= cap.
+ * Waits for peers are bounded (2 s); on expiry *err_flag (device int) is
+ * set to a non-zero code and the output is invalid.
+ */
+TS_API size_t ts_peer_buffer_bytes(int world, int64_t cap);
+TS_API int ts_peer_alloc(int world, int64_t cap, void** ptr);
+TS_API int ts_peer_free(void* ptr);
+TS_API int ts_ipc_get_handle(void* ptr, void* handle_out);
+TS_API int ts_ipc_open(const void* handle, void** ptr);
+TS_API int ts_ipc_close(void* ptr);
+TS_API int ts_allreduce_oneshot(void* const* peer_bufs, int rank, int world, int64_t cap, const float* in,
+                                const float* residual, float* out, int64_t n, int* err_flag, void* stream);
+
 /* Dense reconstruction W[rows, cols] in `out_dtype`.
  * Replaces triton_kernels.py:1114-1186 `dequantize_weight` (which covers only
  * 4/8-bit; this covers 2/4/8 and the double-quantized metadata). With

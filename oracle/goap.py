@@ -231,6 +231,10 @@ class QT:
     dq_gmin_codes: Optional[np.ndarray] = None
     dq_gmin_meta: Optional[np.ndarray] = None
     codebook: Optional[np.ndarray] = None
+    smooth_scale: Optional[np.ndarray] = None
+    stage2_packed: Optional[np.ndarray] = None
+    stage2_scale: Optional[np.ndarray] = None
+    stage2_gmin: Optional[np.ndarray] = None
     # by-products the CUDA quantizer also returns (not QuantizedTensor fields)
     codes: Optional[np.ndarray] = field(default=None, repr=False)
     threshold: Optional[float] = None
@@ -257,9 +261,16 @@ def topk_outliers(flat: np.ndarray, k: int) -> Tuple[np.ndarray, Optional[np.flo
     return idx.astype(np.int64), F32(thr)
 
 
+def smooth_scales(work: np.ndarray, alpha: float) -> np.ndarray:
+    """codec.py:519-523: s_j = max(max_i |w_ij|, 1e-8) ** alpha in float32."""
+    col_max = np.maximum(np.abs(work).max(axis=0), EPS)
+    return np.power(col_max, F32(alpha)).astype(np.float32)
+
+
 def quantize(w: np.ndarray, bits: int = 4, group_size: int = 128, outlier_frac: float = 0.001,
              double_quant: bool = False, dq_group_size: int = 256, mode: str = "uniform",
-             codebook: Optional[np.ndarray] = None, lloyd_sample: Optional[np.ndarray] = None) -> QT:
+             codebook: Optional[np.ndarray] = None, lloyd_sample: Optional[np.ndarray] = None,
+             smooth: bool = False, smooth_alpha: float = 0.5) -> QT:
     """GOAP quantize (codec.py:453-675) of a 2-D array.
 
     mode: "uniform" (round-half-even grid), "nf" (nf_quant=True) or "lloyd"
@@ -268,11 +279,18 @@ def quantize(w: np.ndarray, bits: int = 4, group_size: int = 128, outlier_frac: 
     (flat indices of the normalized values to fit on; all of them when the
     tensor has at most 300,000 elements, as the reference does).
     """
+    if bits == 6:
+        return quantize_rvq(w, group_size, outlier_frac, double_quant, dq_group_size, smooth, smooth_alpha)
     if bits not in (2, 4, 8):
-        raise ValueError("bits must be 2, 4 or 8")
+        raise ValueError("bits must be 2, 4, 6 or 8")
     w = np.asarray(w)
     rows, cols = w.shape
-    work = w.astype(np.float32).reshape(-1).copy()                 # codec.py:517
+    work2 = w.astype(np.float32)                                    # codec.py:517
+    s_smooth = None
+    if smooth:                                                       # codec.py:519-525
+        s_smooth = smooth_scales(work2, smooth_alpha)
+        work2 = work2 / s_smooth[None, :]
+    work = work2.reshape(-1).copy()
     k = n_outliers_for(work.shape[0], outlier_frac)
     idx, thr = topk_outliers(work, k)
     if thr is not None:
@@ -318,7 +336,8 @@ def quantize(w: np.ndarray, bits: int = 4, group_size: int = 128, outlier_frac: 
            n_groups=n_groups, packed=packed, scale=scale16, gmin=gmin16,
            outlier_idx=idx.astype(np.int32), outlier_val=vals.astype(np.float16),
            codebook=cb_store, codes=codes, threshold=None if thr is None else float(thr),
-           assign_codebook_f32=cb_assign)
+           assign_codebook_f32=cb_assign,
+           smooth_scale=None if s_smooth is None else s_smooth.astype(np.float16))
     if double_quant:                                                 # codec.py:644-652
         q.dq_scale_codes, q.dq_scale_meta = double_quantize(scale16, dq_group_size)
         q.dq_gmin_codes, q.dq_gmin_meta = double_quantize(gmin16, dq_group_size)
@@ -351,16 +370,44 @@ def code_values(q) -> np.ndarray:
     return codes.astype(np.float32)
 
 
+def quantize_rvq(w: np.ndarray, group_size: int = 128, outlier_frac: float = 0.001, double_quant: bool = False,
+                 dq_group_size: int = 256, smooth: bool = False, smooth_alpha: float = 0.5) -> QT:
+    """6-bit residual quantization, codec.py:678-737: 4-bit stage (outliers,
+    double quant and smoothing as asked), then the fp32 residual w - W4 at
+    2 bits with no outliers, no smoothing and no double quant."""
+    q4 = quantize(w, 4, group_size, outlier_frac, double_quant, dq_group_size, smooth=smooth,
+                  smooth_alpha=smooth_alpha)
+    res = np.asarray(w).astype(np.float32) - dequantize(q4)
+    q2 = quantize(res, 2, group_size, 0.0)
+    q4.bits = 6
+    q4.stage2_packed, q4.stage2_scale, q4.stage2_gmin = q2.packed, q2.scale, q2.gmin
+    return q4
+
+
 def dequantize(q, exact_outliers: bool = True) -> np.ndarray:
-    """codec.py:761-807: fp32 W [rows, cols]; outlier positions hold the exact
-    stored `outlier_val` (the oracle definition of the weight)."""
+    """codec.py:761-807, 810-847: fp32 W [rows, cols]; outlier positions hold
+    the exact stored `outlier_val` (the oracle definition of the weight);
+    columns multiplied back by the smooth scales; 6-bit: plus the 2-bit
+    residual stage."""
+    if q.bits == 6:
+        s1 = QT(rows=q.rows, cols=q.cols, bits=4, group_size=q.group_size, padded_cols=q.padded_cols,
+                n_groups=q.n_groups, packed=q.packed, scale=q.scale, gmin=q.gmin, outlier_idx=q.outlier_idx,
+                outlier_val=q.outlier_val, dq_scale_codes=q.dq_scale_codes, dq_scale_meta=q.dq_scale_meta,
+                dq_gmin_codes=q.dq_gmin_codes, dq_gmin_meta=q.dq_gmin_meta, smooth_scale=q.smooth_scale)
+        s2 = QT(rows=q.rows, cols=q.cols, bits=2, group_size=q.group_size, padded_cols=q.padded_cols,
+                n_groups=q.n_groups, packed=q.stage2_packed, scale=q.stage2_scale, gmin=q.stage2_gmin,
+                outlier_idx=np.zeros(0, np.int32), outlier_val=np.zeros(0, np.float16))
+        return dequantize(s1, exact_outliers) + dequantize(s2)
     cv = code_values(q).reshape(q.rows, q.n_groups, q.group_size)
     s, m = resolve_scale_gmin(q)
     deq = (cv * s[..., None] + m[..., None]).reshape(q.rows, q.padded_cols)[:, : q.cols]
     flat = deq.reshape(-1).copy()
     if exact_outliers and q.outlier_idx.shape[0]:
         flat[q.outlier_idx.astype(np.int64)] = q.outlier_val.astype(np.float32)
-    return flat.reshape(q.rows, q.cols)
+    out = flat.reshape(q.rows, q.cols)
+    if getattr(q, "smooth_scale", None) is not None:
+        out = out * q.smooth_scale.astype(np.float32)[None, :]
+    return out
 
 
 @dataclass

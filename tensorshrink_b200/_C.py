@@ -80,6 +80,13 @@ _SIGNATURES = [
                                               _vp, _i64, _vp]),
     ("ts_outlier_tables_from_stream", C.c_int, [C.POINTER(TsQWeight), _vp, _vp, C.c_int, _vp, _i64, _vp, _vp,
                                                 _vp, _vp, _vp, _vp]),
+    ("ts_peer_buffer_bytes", C.c_size_t, [C.c_int, _i64]),
+    ("ts_peer_alloc", C.c_int, [C.c_int, _i64, C.POINTER(_vp)]),
+    ("ts_peer_free", C.c_int, [_vp]),
+    ("ts_ipc_get_handle", C.c_int, [_vp, _vp]),
+    ("ts_ipc_open", C.c_int, [_vp, C.POINTER(_vp)]),
+    ("ts_ipc_close", C.c_int, [_vp]),
+    ("ts_allreduce_oneshot", C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
     ("ts_dequantize_weight", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, C.c_int, _vp]),
     ("ts_quantize_workspace_size", C.c_size_t, [C.POINTER(TsQuantParams)]),
     ("ts_quantize_pack", C.c_int, [_vp, C.c_int, C.POINTER(TsQuantParams), C.POINTER(TsQuantOutputs),

@@ -167,6 +167,10 @@ class DeviceQuant:
     dq_group_size: int = 0
     codebook_assign: Optional[torch.Tensor] = None  # fp32 levels the codes were assigned against
     codebook_store: Optional[torch.Tensor] = None   # what QuantizedTensor.codebook holds
+    smooth_scale: Optional[torch.Tensor] = None     # fp16 [cols] column scales (smooth=True)
+    stage2_packed: Optional[torch.Tensor] = None    # 6-bit RVQ: 2-bit residual stage
+    stage2_scale: Optional[torch.Tensor] = None
+    stage2_gmin: Optional[torch.Tensor] = None
 
     def to_quantized_tensor(self) -> QuantizedTensor:
         def h(t):
@@ -179,7 +183,9 @@ class DeviceQuant:
             outlier_idx=h(self.outlier_idx), outlier_val=h(self.outlier_val),
             dq_scale_codes=h(self.dq_scale_codes), dq_scale_meta=h(self.dq_scale_meta),
             dq_gmin_codes=h(self.dq_gmin_codes), dq_gmin_meta=h(self.dq_gmin_meta),
-            codebook=h(self.codebook_store))
+            codebook=h(self.codebook_store), smooth_scale=h(self.smooth_scale),
+            stage2_packed=h(self.stage2_packed), stage2_scale=h(self.stage2_scale),
+            stage2_gmin=h(self.stage2_gmin))
 
 
 def n_outliers_for(n_elem: int, outlier_frac: float) -> int:
@@ -200,7 +206,8 @@ def quantize_device(w: torch.Tensor, bits: int = 4, group_size: int = DEFAULT_GR
                     dq_group_size: int = DEFAULT_DQ_GROUP_SIZE, companded: bool = False,
                     nf_quant: bool = False, codebook: Optional[torch.Tensor] = None,
                     lloyd_sample: Optional[torch.Tensor] = None,
-                    lloyd_iters: int = DEFAULT_COMPAND_ITERS) -> DeviceQuant:
+                    lloyd_iters: int = DEFAULT_COMPAND_ITERS, smooth: bool = False,
+                    smooth_alpha: float = DEFAULT_SMOOTH_ALPHA) -> DeviceQuant:
     """GOAP quantize on the GPU (codec.py:453-675 semantics; bits 2/4/8).
 
     companded=True fits a Lloyd-Max codebook on the device (codec.py:320-361)
@@ -209,10 +216,19 @@ def quantize_device(w: torch.Tensor, bits: int = 4, group_size: int = DEFAULT_GR
     (codec.py:329-333). `lloyd_sample` (int64 flat indices into the padded
     [rows, padded_cols] grid) or `codebook` (sorted fp32 levels to assign
     against, skipping the fit) override that.
+
+    smooth=True (codec.py:519-525) divides each column by
+    s_j = max(max_i |w_ij|, 1e-8) ** smooth_alpha before quantizing and keeps
+    f16(s) as `smooth_scale`; the column maxima come from the device and the
+    power is taken by torch on the host, as the reference computes it, so
+    the scales (and the codes) are the reference's. bits=6 is the residual
+    scheme of codec.py:678-737 (`quantize_rvq_device`).
     """
+    if bits == 6:
+        if companded:
+            raise ValueError("companded=True is not supported with bits=6 (RVQ)")
+        return quantize_rvq_device(w, group_size, outlier_frac, double_quant, dq_group_size, smooth, smooth_alpha)
     if bits not in (2, 4, 8):
-        if bits == 6:
-            raise NotImplementedError("bits=6 (RVQ) has no GPU quantizer in tensorshrink_b200")
         raise ValueError("bits must be 2, 4, 6, or 8")
     if w.dim() < 2:
         raise ValueError("quantize_tensor expects a tensor with ndim >= 2")
@@ -225,6 +241,13 @@ def quantize_device(w: torch.Tensor, bits: int = 4, group_size: int = DEFAULT_GR
     w2d = w.detach().reshape(rows, cols)
     if w2d.dtype not in (torch.float16, torch.bfloat16, torch.float32):
         w2d = w2d.to(torch.float32)
+    smooth16 = None
+    if smooth:
+        work = w2d.to(torch.float32)
+        col_max = work.abs().amax(dim=0).clamp(min=_EPS)
+        s_j = col_max.cpu().pow(smooth_alpha).to(dev)
+        w2d = work / s_j.unsqueeze(0)
+        smooth16 = s_j.to(torch.float16)
     w2d = w2d.contiguous()
     gs = int(group_size)
     padded_cols = (cols + gs - 1) // gs * gs
@@ -316,7 +339,24 @@ def quantize_device(w: torch.Tensor, bits: int = 4, group_size: int = DEFAULT_GR
         padded_cols=padded_cols, n_groups=n_groups, packed=packed, scale=scale, gmin=gmin,
         outlier_idx=idx, outlier_val=val, outlier_row=orow, outlier_col=ocol, outlier_delta=odelta,
         outlier_row_ptr=optr, threshold=thr, dq_group_size=int(dq_group_size) if double_quant else 0,
-        codebook_assign=cb_assign, codebook_store=cb_store, **dq)
+        codebook_assign=cb_assign, codebook_store=cb_store, smooth_scale=smooth16, **dq)
+
+
+def quantize_rvq_device(w: torch.Tensor, group_size: int = DEFAULT_GROUP_SIZE,
+                        outlier_frac: float = DEFAULT_OUTLIER_FRAC, double_quant: bool = False,
+                        dq_group_size: int = DEFAULT_DQ_GROUP_SIZE, smooth: bool = False,
+                        smooth_alpha: float = DEFAULT_SMOOTH_ALPHA) -> DeviceQuant:
+    """6-bit residual quantization on the GPU (codec.py:678-737): a 4-bit
+    stage with outliers (and double quant / smoothing as asked), then the
+    fp32 residual w - W4 quantized at 2 bits without outliers."""
+    w = _as_cuda(w)
+    d4 = quantize_device(w, bits=4, group_size=group_size, outlier_frac=outlier_frac, double_quant=double_quant,
+                         dq_group_size=dq_group_size, smooth=smooth, smooth_alpha=smooth_alpha)
+    residual = w.detach().reshape(d4.rows, d4.cols).to(torch.float32) - dequantize_device(d4).reshape(d4.rows, -1)
+    d2 = quantize_device(residual, bits=2, group_size=group_size, outlier_frac=0.0)
+    d4.bits = 6
+    d4.stage2_packed, d4.stage2_scale, d4.stage2_gmin = d2.packed, d2.scale, d2.gmin
+    return d4
 
 
 def quantize_tensor(
@@ -332,16 +372,14 @@ def quantize_tensor(
     nf_quant: bool = False,
 ) -> QuantizedTensor:
     """GOAP quantize (codec.py:453-675) on the GPU, returning a host
-    QuantizedTensor. `smooth` and bits=6 (RVQ) are not implemented."""
-    if smooth:
-        raise NotImplementedError("smooth=True is not implemented by tensorshrink_b200")
-    if bits == 6:
-        raise NotImplementedError("bits=6 (RVQ) is not implemented by tensorshrink_b200")
+    QuantizedTensor; smooth scaling and 6-bit RVQ included."""
+    if bits == 6 and companded:
+        raise ValueError("companded=True is not supported with bits=6 (RVQ)")
     if companded and nf_quant:
         nf_quant = False  # codec.py:582: nf_quant applies only when not companded
     dq = quantize_device(w, bits=bits, group_size=group_size, outlier_frac=outlier_frac,
                          double_quant=double_quant, dq_group_size=dq_group_size,
-                         companded=companded, nf_quant=nf_quant)
+                         companded=companded, nf_quant=nf_quant, smooth=smooth, smooth_alpha=smooth_alpha)
     return dq.to_quantized_tensor()
 
 
@@ -364,12 +402,33 @@ def _qt_device_tensors(qt: QuantizedTensor, device: torch.device) -> dict:
     return d
 
 
+def _reconstruct(bits, rows, cols, padded_cols, n_groups, group_size, packed, scale, gmin, codebook=None,
+                 dq_scale_codes=None, dq_scale_meta=None, dq_gmin_codes=None, dq_gmin_meta=None,
+                 dq_group_size=0, outlier_idx=None, outlier_val=None, smooth_scale=None, stage2=None):
+    """fp32 W [rows, cols] on the device from device tensors: the group-affine
+    stage (the 4-bit stage when bits == 6) with exact outlier values, columns
+    multiplied back by the smooth scales, plus the 2-bit residual stage of a
+    6-bit tensor (codec.py:761-847)."""
+    dq = dq_scale_codes is not None
+    W = _dequantize_weight(packed, None if dq else scale, None if dq else gmin, 4 if bits == 6 else bits, rows,
+                           cols, padded_cols, n_groups, group_size, torch.float32, codebook=codebook,
+                           dq_scale_codes=dq_scale_codes, dq_scale_meta=dq_scale_meta,
+                           dq_gmin_codes=dq_gmin_codes, dq_gmin_meta=dq_gmin_meta, dq_group_size=dq_group_size)
+    if outlier_idx is not None and outlier_idx.numel():
+        W.view(-1)[outlier_idx.to(torch.int64)] = outlier_val.to(torch.float32)
+    if smooth_scale is not None:
+        W = W * smooth_scale.to(torch.float32).unsqueeze(0)
+    if bits == 6:
+        p2, s2, g2 = stage2
+        W = W + _dequantize_weight(p2, s2, g2, 2, rows, cols, padded_cols, n_groups, group_size, torch.float32)
+    return W
+
+
 def dequantize_tensor(qt: QuantizedTensor, device=None, dtype=None) -> torch.Tensor:
-    """codec.py:761-807 on the GPU: fp32 reconstruction (double-quant metadata
-    in fp32), exact `outlier_val` at outlier positions, then cast to `dtype`
-    and moved to `device` (default "cpu", as the reference)."""
-    if qt.bits == 6 or qt.smooth_scale is not None:
-        raise NotImplementedError("RVQ / smooth-scaled tensors are not implemented by tensorshrink_b200")
+    """codec.py:761-847 on the GPU: fp32 reconstruction (double-quant metadata
+    in fp32), exact `outlier_val` at outlier positions, smooth scales and the
+    6-bit residual stage applied, then cast to `dtype` and moved to `device`
+    (default "cpu", as the reference)."""
     device = torch.device(device or "cpu")
     out_dtype = dtype or getattr(torch, qt.orig_dtype, torch.float16)
     gdev = device if device.type == "cuda" else torch.device("cuda", torch.cuda.current_device()) \
@@ -377,30 +436,22 @@ def dequantize_tensor(qt: QuantizedTensor, device=None, dtype=None) -> torch.Ten
     if gdev is None:
         raise RuntimeError("tensorshrink_b200 dequantizes on the GPU; no CUDA device is available")
     d = _qt_device_tensors(qt, gdev)
-    W = _dequantize_weight(
-        d["packed"], d.get("scale"), d.get("gmin"), qt.bits, qt.rows, qt.cols, qt.padded_cols,
-        qt.n_groups, qt.group_size, torch.float32, codebook=d["codebook"],
-        dq_scale_codes=d.get("dq_scale_codes"), dq_scale_meta=d.get("dq_scale_meta"),
-        dq_gmin_codes=d.get("dq_gmin_codes"), dq_gmin_meta=d.get("dq_gmin_meta"),
-        dq_group_size=d.get("dq_group_size", 0))
-    if qt.n_outliers() > 0:
-        idx = torch.from_numpy(qt.outlier_idx.astype(np.int64)).to(gdev)
-        val = torch.from_numpy(qt.outlier_val).to(gdev).to(torch.float32)
-        W.view(-1)[idx] = val
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(gdev)  # noqa: E731
+    stage2 = (t(qt.stage2_packed), t(qt.stage2_scale), t(qt.stage2_gmin)) if qt.bits == 6 else None
+    W = _reconstruct(qt.bits, qt.rows, qt.cols, qt.padded_cols, qt.n_groups, qt.group_size, d["packed"],
+                     d.get("scale"), d.get("gmin"), d["codebook"], d.get("dq_scale_codes"), d.get("dq_scale_meta"),
+                     d.get("dq_gmin_codes"), d.get("dq_gmin_meta"), d.get("dq_group_size", 0),
+                     t(qt.outlier_idx.astype(np.int64)), t(qt.outlier_val), t(qt.smooth_scale), stage2)
     return W.reshape(qt.orig_shape).to(device=device, dtype=out_dtype)
 
 
 def dequantize_device(dq: DeviceQuant, dtype=torch.float32) -> torch.Tensor:
     """Dense reconstruction of a DeviceQuant (exact outlier values)."""
-    W = _dequantize_weight(
-        dq.packed, None if dq.dq_scale_codes is not None else dq.scale,
-        None if dq.dq_scale_codes is not None else dq.gmin, dq.bits, dq.rows, dq.cols,
-        dq.padded_cols, dq.n_groups, dq.group_size, torch.float32,
-        codebook=None if dq.codebook_store is None else dq.codebook_store.to(torch.float32),
-        dq_scale_codes=dq.dq_scale_codes, dq_scale_meta=dq.dq_scale_meta,
-        dq_gmin_codes=dq.dq_gmin_codes, dq_gmin_meta=dq.dq_gmin_meta, dq_group_size=dq.dq_group_size)
-    if dq.outlier_idx.numel():
-        W.view(-1)[dq.outlier_idx.to(torch.int64)] = dq.outlier_val.to(torch.float32)
+    W = _reconstruct(dq.bits, dq.rows, dq.cols, dq.padded_cols, dq.n_groups, dq.group_size, dq.packed, dq.scale,
+                     dq.gmin, None if dq.codebook_store is None else dq.codebook_store.to(torch.float32),
+                     dq.dq_scale_codes, dq.dq_scale_meta, dq.dq_gmin_codes, dq.dq_gmin_meta, dq.dq_group_size,
+                     dq.outlier_idx, dq.outlier_val, dq.smooth_scale,
+                     (dq.stage2_packed, dq.stage2_scale, dq.stage2_gmin) if dq.bits == 6 else None)
     return W.reshape(dq.orig_shape).to(dtype)
 
 
@@ -439,21 +490,22 @@ def quantize_tensor_adaptive(
     qd, err, esc = quantize_device_adaptive(
         w, group_size=group_size, outlier_frac=outlier_frac, error_threshold=error_threshold,
         force_bits=force_bits, double_quant=double_quant, dq_group_size=dq_group_size,
-        smooth=smooth, allowed_bits=allowed_bits, companded=companded, nf_quant=nf_quant)
+        smooth=smooth, smooth_alpha=smooth_alpha, allowed_bits=allowed_bits, companded=companded,
+        nf_quant=nf_quant)
     return qd.to_quantized_tensor(), err, esc
 
 
 def quantize_device_adaptive(w, group_size=DEFAULT_GROUP_SIZE, outlier_frac=DEFAULT_OUTLIER_FRAC,
                              error_threshold=DEFAULT_ERROR_THRESHOLD, force_bits=None,
                              double_quant=False, dq_group_size=DEFAULT_DQ_GROUP_SIZE, smooth=False,
-                             allowed_bits=DEFAULT_ADAPTIVE_BIT_CHAIN, companded=False, nf_quant=False):
+                             allowed_bits=DEFAULT_ADAPTIVE_BIT_CHAIN, companded=False, nf_quant=False,
+                             smooth_alpha=DEFAULT_SMOOTH_ALPHA):
     """Device-resident variant of quantize_tensor_adaptive."""
-    if smooth:
-        raise NotImplementedError("smooth=True is not implemented by tensorshrink_b200")
     if companded and (force_bits == 6 or 6 in tuple(allowed_bits)):
         raise ValueError("companded=True is not supported with bits=6 (RVQ)")
     kw = dict(group_size=group_size, outlier_frac=outlier_frac, double_quant=double_quant,
-              dq_group_size=dq_group_size, companded=companded, nf_quant=nf_quant and not companded)
+              dq_group_size=dq_group_size, companded=companded, nf_quant=nf_quant and not companded,
+              smooth=smooth, smooth_alpha=smooth_alpha)
     if force_bits is not None:
         qd = quantize_device(w, bits=force_bits, **kw)
         return qd, relative_error(w, qd), False

@@ -309,30 +309,84 @@ __global__ void __launch_bounds__(kThreads) cta_hist_kernel(const Geometry g, co
 }
 
 // ---- select: threshold, per-CTA offsets and tie shares ----------------------
-__global__ void finalize_select_kernel(const uint32_t* cta_hist, int nb, int n_cta, SelState* st,
-                                       int64_t* cta_info /* [n_cta][2] offset, tie_take */,
-                                       int key_bits, int dtype) {
+// One block of 1024 threads (n_cta <= 1024 by the CTA plan). The bin totals
+// are summed by (bin, CTA slice) pairs; the threshold bin is found by one
+// thread walking at most 1024 bins in shared memory; each thread then counts
+// one CTA's elements above the threshold and ties at it, and two block-wide
+// exclusive scans turn those into output offsets and tie shares (ties are
+// granted in CTA order, i.e. lowest flat indices first).
+constexpr int kSelThreads = 1024;
+
+__device__ __forceinline__ int64_t block_excl_scan64(int64_t v, int64_t* warp_tot /* [32] */) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int64_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) warp_tot[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int64_t w = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t t = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += t;
+    }
+    warp_tot[lane] = w;   // inclusive prefix over warps
+  }
+  __syncthreads();
+  const int64_t r = incl - v + (wid > 0 ? warp_tot[wid - 1] : 0);
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kSelThreads) finalize_select_kernel(const uint32_t* cta_hist, int nb, int n_cta,
+                                                                      SelState* st,
+                                                                      int64_t* cta_info /* [n_cta][2] */,
+                                                                      int key_bits, int dtype) {
   extern __shared__ uint32_t tot[];  // nb
-  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-    uint32_t s = 0;
-    for (int c = 0; c < n_cta; ++c) s += cta_hist[(size_t)c * (nb + 1) + b];
-    tot[b] = s;
+  __shared__ int64_t warp_tot[32];
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) tot[b] = 0;
+  __syncthreads();
+  {
+    const int slices = blockDim.x >= (unsigned)nb ? (int)blockDim.x / nb : 1;
+    const int b = threadIdx.x % nb, sl = threadIdx.x / nb;
+    if (sl < slices) {
+      uint32_t sum = 0;
+      for (int c = sl; c < n_cta; c += slices) sum += cta_hist[(size_t)c * (nb + 1) + b];
+      atomicAdd(&tot[b], sum);
+    }
+    for (int bb = b + slices * nb; bb < nb; bb += blockDim.x) {   // nb > blockDim: remaining bins
+      uint32_t sum2 = 0;
+      for (int c = 0; c < n_cta; ++c) sum2 += cta_hist[(size_t)c * (nb + 1) + bb];
+      atomicAdd(&tot[bb], sum2);
+    }
   }
   __syncthreads();
   int bin;
   int64_t above_in_level;
   select_bin(tot, nb, st->k_rem, &bin, &above_in_level);
-  // Per CTA: elements above T and ties at T, counted by all threads (one CTA
-  // per thread at a time) into cta_info, then turned into output offsets and
-  // tie shares by one running prefix (ties are granted in CTA order).
-  for (int c = threadIdx.x; c < n_cta; c += blockDim.x) {
+  const int64_t need = st->k_rem - above_in_level;  // ties needed within the bin
+  int64_t gt = 0, eq = 0;
+  const int c = threadIdx.x;
+  if (c < n_cta) {
     const uint32_t* h = cta_hist + (size_t)c * (nb + 1);
-    int64_t gt = h[nb];
+    gt = h[nb];
+#pragma unroll 8
     for (int b = bin + 1; b < nb; ++b) gt += h[b];
-    cta_info[2 * c] = gt;
-    cta_info[2 * c + 1] = h[bin];
+    eq = h[bin];
   }
-  __syncthreads();
+  const int64_t eq_before = block_excl_scan64(eq, warp_tot);
+  const int64_t take = i64max(0, i64min(eq, need - eq_before));
+  const int64_t off = block_excl_scan64(gt + take, warp_tot);
+  const int64_t n_gt_before = block_excl_scan64(gt, warp_tot);
+  if (c < n_cta) {
+    cta_info[2 * c] = off;
+    cta_info[2 * c + 1] = take;
+  }
+  if (c == n_cta - 1) st->n_gt = n_gt_before + gt;
   if (threadIdx.x == 0) {
     const uint32_t tkey = (st->prefix << (31 - __clz(nb))) | (uint32_t)bin;
     st->t_key = tkey;
@@ -343,21 +397,7 @@ __global__ void finalize_select_kernel(const uint32_t* cta_hist, int nb, int n_c
     else
       st->t_val = __uint_as_float(tkey);
     (void)key_bits;
-    // k = n_gt + need_eq
-    const int64_t need = st->k_rem - above_in_level;  // ties needed within the bin
     st->need_eq = need;
-    int64_t off = 0, eq_before = 0, n_gt = 0;
-    for (int c = 0; c < n_cta; ++c) {
-      const int64_t gt = cta_info[2 * c];
-      const int64_t eq = cta_info[2 * c + 1];
-      const int64_t take = i64max(0, i64min(eq, need - eq_before));
-      eq_before += eq;
-      n_gt += gt;
-      cta_info[2 * c] = off;
-      cta_info[2 * c + 1] = take;
-      off += gt + take;
-    }
-    st->n_gt = n_gt;
   }
 }
 
@@ -952,8 +992,9 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
     cta_hist_kernel<DT><<<plan.n_cta, kThreads, 0, stream>>>(g, plan, st, cta_hist);
     TS_LAUNCH_CHECK();
     const int nb = 1 << E::LAST_BITS;
-    finalize_select_kernel<<<1, 256, nb * sizeof(uint32_t), stream>>>(cta_hist, nb, plan.n_cta, st, cta_info,
-                                                                      E::KEY_BITS, DT);
+    TS_REQUIRE(plan.n_cta <= kSelThreads, "quantize_pack: %d row ranges exceed the select block", plan.n_cta);
+    finalize_select_kernel<<<1, kSelThreads, nb * sizeof(uint32_t), stream>>>(cta_hist, nb, plan.n_cta, st,
+                                                                              cta_info, E::KEY_BITS, DT);
     TS_LAUNCH_CHECK();
   }
   if (o.threshold) {

@@ -97,10 +97,10 @@ def _group_info(group):
     return 1, 0
 
 
-def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    xf = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
-    return (xf * w.float()).to(x.dtype)
+def _rms_norm(h: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm of the fp32 residual stream `h` with fp32 weights, to bf16
+    (the projections' activation dtype)."""
+    return F.rms_norm(h, (h.shape[-1],), w, eps).to(torch.bfloat16)
 
 
 class ShardedProjection(nn.Module):
@@ -121,6 +121,23 @@ class ShardedProjection(nn.Module):
             c0, c1 = tp.shard_bounds(ql.padded_cols, world, rank, ql.group_size)
             self.lo, self.hi = c0, min(c1, ql.cols)
             self.local = tp.shard_cols(ql, self.lo, self.hi)
+
+    def forward(self, x: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        from . import kernels
+        x2d = x.reshape(-1, x.shape[-1])
+        if not x2d.is_contiguous():
+            x2d = x2d.contiguous()
+        y = kernels.qlinear(x2d, self.local.qweight(), self.local.bias, out_dtype or x.dtype)
+        return y.reshape(*x.shape[:-1], y.shape[-1])
+
+
+class FusedProjection(nn.Module):
+    """A QuantLinear called through kernels.qlinear (rows of several
+    projections)."""
+
+    def __init__(self, ql: QuantLinear):
+        super().__init__()
+        self.local = ql
 
     def forward(self, x: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
         from . import kernels
@@ -154,12 +171,20 @@ class QuantDecoderLayer(nn.Module):
             del ql, dq
         self.n_heads_local = cfg.n_heads // world
         self.n_kv_local = cfg.n_kv_heads // world
-        self.input_norm = nn.Parameter(torch.ones(H, dtype=torch.bfloat16, device=device), requires_grad=False)
-        self.post_norm = nn.Parameter(torch.ones(H, dtype=torch.bfloat16, device=device), requires_grad=False)
+        # this rank's q/k/v and gate/up shards fused into one launch each
+        # (rows concatenated; every row reconstructs exactly as before)
+        from .tp import concat_rows
+        self.qkv = FusedProjection(concat_rows([self.q_proj.local, self.k_proj.local, self.v_proj.local]))
+        self.gate_up = FusedProjection(concat_rows([self.gate_proj.local, self.up_proj.local]))
+        self.splits_qkv = [self.q_proj.local.rows, self.k_proj.local.rows, self.v_proj.local.rows]
+        self.split_gate = self.gate_proj.local.rows
+        del self.q_proj, self.k_proj, self.v_proj, self.gate_proj, self.up_proj
+        self.input_norm = nn.Parameter(torch.ones(H, dtype=torch.float32, device=device), requires_grad=False)
+        self.post_norm = nn.Parameter(torch.ones(H, dtype=torch.float32, device=device), requires_grad=False)
 
     def projections(self):
-        return [self.q_proj, self.k_proj, self.v_proj, self.o_proj, self.gate_proj, self.up_proj,
-                self.down_proj]
+        """The layers one forward runs (fused q/k/v and gate/up)."""
+        return [self.qkv, self.o_proj, self.gate_up, self.down_proj]
 
 
 class QuantDecoder(nn.Module):
@@ -180,8 +205,12 @@ class QuantDecoder(nn.Module):
         # embed / lm_head stay unquantized (the reference skips them by name)
         self.embed = (torch.randn(cfg.vocab, H, generator=g, device=self.device) * 0.02).to(torch.bfloat16)
         v0, v1 = self._vocab_bounds(self.rank)
-        self.lm_head = (torch.randn(v1 - v0, H, generator=g, device=self.device) * 0.02).to(torch.bfloat16)
-        self.final_norm = torch.ones(H, dtype=torch.bfloat16, device=self.device)
+        # every rank draws the whole head and keeps its vocabulary slice, so
+        # the sharded model is the unsharded one cut up
+        full = (torch.randn(cfg.vocab, H, generator=g, device=self.device) * 0.02).to(torch.bfloat16)
+        self.lm_head = full[v0:v1].contiguous()
+        del full
+        self.final_norm = torch.ones(H, dtype=torch.float32, device=self.device)
         self.layer_bits = cfg.bits_per_layer()
         self.layers = nn.ModuleList(
             QuantDecoderLayer(cfg, i, b, self.device, self.world, self.rank) for i, b in enumerate(self.layer_bits))
@@ -206,13 +235,15 @@ class QuantDecoder(nn.Module):
         return sum(p.local.packed_nbytes() for layer in self.layers for p in layer.projections())
 
     # -- pieces -------------------------------------------------------------------------
-    def _all_reduce(self, y: torch.Tensor) -> torch.Tensor:
+    def _reduce_add(self, partial: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        """h + the sum over ranks of a row-parallel fp32 partial."""
         if self.world == 1:
-            return y
-        if self.exchange is not None:
-            return self.exchange.all_reduce(y)
-        dist.all_reduce(y, group=self.group)
-        return y
+            return h + partial
+        if self.exchange is not None and partial.numel() <= self.exchange.cap:
+            # decode-sized exchanges: the one-shot kernel (residual add fused)
+            return self.exchange.all_reduce(partial.contiguous(), residual=h.contiguous())
+        dist.all_reduce(partial, group=self.group)
+        return h + partial
 
     def _rope(self, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         # x [B, T, h, D]; pos [T] absolute positions
@@ -222,36 +253,33 @@ class QuantDecoder(nn.Module):
         return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1).to(x.dtype)
 
     def _layer(self, i: int, layer: QuantDecoderLayer, h: torch.Tensor, pos: torch.Tensor,
-               n_ctx: Optional[torch.Tensor], attn_len: int = 0) -> torch.Tensor:
+               mask: Optional[torch.Tensor], attn_len: int = 0) -> torch.Tensor:
         cfg = self.cfg
         B, T, _ = h.shape
         D = cfg.head_dim
         x = _rms_norm(h, layer.input_norm, cfg.rms_eps)
-        q = layer.q_proj(x).view(B, T, layer.n_heads_local, D)
-        k = layer.k_proj(x).view(B, T, layer.n_kv_local, D)
-        v = layer.v_proj(x).view(B, T, layer.n_kv_local, D)
-        q, k = self._rope(q, pos), self._rope(k, pos)
+        q, k, v = layer.qkv(x).split(layer.splits_qkv, dim=-1)
+        q = self._rope(q.view(B, T, layer.n_heads_local, D), pos)
+        k = self._rope(k.view(B, T, layer.n_kv_local, D), pos)
+        v = v.view(B, T, layer.n_kv_local, D)
         kc, vc = self.k_cache[i, :B], self.v_cache[i, :B]
         kc.index_copy_(2, pos, k.transpose(1, 2))
         vc.index_copy_(2, pos, v.transpose(1, 2))
-        if n_ctx is None:
+        if mask is None:
             # prefill from position 0: causal attention over the T new tokens
             a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                                is_causal=True, enable_gqa=True)
         else:
-            # decode: attend to cache positions < n_ctx (a device tensor, so the
-            # step is the same CUDA graph at every position)
-            L = attn_len or self.max_seq
-            mask = (torch.arange(L, device=h.device) < n_ctx)[None, None, None, :]
+            # decode: attend to the first L cache positions, masked to < pos + 1
+            # (a device-side mask, so every position replays the same graph)
+            L = mask.shape[-1]
             a = F.scaled_dot_product_attention(q.transpose(1, 2), kc[:, :, :L], vc[:, :, :L], attn_mask=mask,
                                                enable_gqa=True)
         a = a.transpose(1, 2).reshape(B, T, layer.n_heads_local * D)
-        o = self._all_reduce(layer.o_proj(a, torch.float32))
-        h = (h.float() + o).to(h.dtype)
+        h = self._reduce_add(layer.o_proj(a, torch.float32), h)
         x = _rms_norm(h, layer.post_norm, cfg.rms_eps)
-        m = F.silu(layer.gate_proj(x)) * layer.up_proj(x)
-        d = self._all_reduce(layer.down_proj(m, torch.float32))
-        return (h.float() + d).to(h.dtype)
+        g, u = layer.gate_up(x).split([layer.split_gate, layer.split_gate], dim=-1)
+        return self._reduce_add(layer.down_proj(F.silu(g) * u, torch.float32), h)
 
     def _next_token(self, h_last: torch.Tensor) -> torch.Tensor:
         """Greedy next token: global argmax over the vocabulary shards."""
@@ -269,19 +297,10 @@ class QuantDecoder(nn.Module):
         return allp[best, torch.arange(pair.shape[0], device=pair.device), 1].long()
 
     # -- entry points ------------------------------------------------------------------
-    @torch.no_grad()
-    def prefill(self, tokens: torch.Tensor, return_logits: bool = False) -> torch.Tensor:
-        """Run `tokens` [B, T] from position 0; fills the KV cache; returns the
-        greedy next token [B], or with `return_logits` the fp32 logits [B, vocab]
-        of the last position (gathered over the vocabulary shards)."""
-        B, T = tokens.shape
-        pos = torch.arange(T, device=tokens.device)
-        h = self.embed[tokens]
-        for i, layer in enumerate(self.layers):
-            h = self._layer(i, layer, h, pos, None)
-        if not return_logits:
-            return self._next_token(h[:, -1])
-        x = _rms_norm(h[:, -1], self.final_norm, self.cfg.rms_eps)
+    def _logits(self, h_last: torch.Tensor) -> torch.Tensor:
+        """fp32 logits [B, vocab] of the last position (gathered over the
+        vocabulary shards)."""
+        x = _rms_norm(h_last, self.final_norm, self.cfg.rms_eps)
         logits = F.linear(x, self.lm_head).float()
         if self.world == 1:
             return logits
@@ -293,16 +312,30 @@ class QuantDecoder(nn.Module):
         return torch.cat(parts, dim=-1)[:, : self.cfg.vocab]
 
     @torch.no_grad()
-    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, attn_len: int = 0) -> torch.Tensor:
+    def prefill(self, tokens: torch.Tensor, return_logits: bool = False) -> torch.Tensor:
+        """Run `tokens` [B, T] from position 0; fills the KV cache; returns the
+        greedy next token [B], or with `return_logits` the last position's
+        fp32 logits [B, vocab]."""
+        B, T = tokens.shape
+        pos = torch.arange(T, device=tokens.device)
+        h = self.embed[tokens].float()
+        for i, layer in enumerate(self.layers):
+            h = self._layer(i, layer, h, pos, None)
+        return self._logits(h[:, -1]) if return_logits else self._next_token(h[:, -1])
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, attn_len: int = 0,
+                    return_logits: bool = False) -> torch.Tensor:
         """One token per sequence: `tokens` [B] at position `pos` (a one-element
         int64 device tensor, advanced by the caller). Attention reads the first
-        `attn_len` cache positions (default all), masked to those < pos + 1.
-        Returns the next tokens."""
-        h = self.embed[tokens][:, None, :]
-        n_ctx = pos + 1
+        `attn_len` cache positions (default all), masked to those <= pos.
+        Returns the next tokens (or the fp32 logits)."""
+        h = self.embed[tokens][:, None, :].float()
+        L = attn_len or self.max_seq
+        mask = (torch.arange(L, device=h.device) <= pos)[None, None, None, :]
         for i, layer in enumerate(self.layers):
-            h = self._layer(i, layer, h, pos, n_ctx, attn_len)
-        return self._next_token(h[:, 0])
+            h = self._layer(i, layer, h, pos, mask, L)
+        return self._logits(h[:, 0]) if return_logits else self._next_token(h[:, 0])
 
 
 class CUDAGraphDecoder:

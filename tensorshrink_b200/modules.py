@@ -130,6 +130,11 @@ class QuantLinear(nn.Module):
             raise ValueError("QuantLinear needs a QuantizedTensor")
         if len(src.orig_shape) != 2:
             raise ValueError("QuantLinear requires a 2D weight (out_features, in_features)")
+        if int(src.bits) == 6 or getattr(src, "smooth_scale", None) is not None:
+            # as in the reference (modules.py:963-969): 6-bit RVQ and smooth-scaled
+            # tensors are storage formats of the codec, not QuantLinear layouts
+            raise ValueError("QuantLinear serves 2/4/8-bit unsmoothed weights; 6-bit RVQ and smooth-scaled "
+                             "tensors are codec-level (quantize_tensor / dequantize_tensor)")
         self.out_features, self.in_features = int(src.orig_shape[0]), int(src.orig_shape[1])
         self.bits = int(src.bits)
         self.group_size = int(src.group_size)
@@ -197,6 +202,14 @@ class QuantLinear(nn.Module):
             self.bias = None
 
     # -- device plumbing ------------------------------------------------------
+    def __getstate__(self):
+        # the cached ts_qweight holds raw device pointers: never copy or pickle it
+        state = super().__getstate__() if hasattr(super(), "__getstate__") else self.__dict__.copy()
+        state = dict(state)
+        state["_qw"] = None
+        state["_qw_key"] = None
+        return state
+
     def _apply(self, fn, recurse=True):
         result = super()._apply(fn, recurse=recurse)
         self._qw = None

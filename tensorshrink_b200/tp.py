@@ -119,8 +119,16 @@ def shard_cols(ql: QuantLinear, c0: int, c1: int) -> QuantLinear:
         # over when each super-group is a whole number of full rows
         gsz, ng = ql.dq_group_size, ql.n_groups
         if gsz % ng:
-            raise ValueError(f"double-quant super-groups of {gsz} entries do not cover whole rows "
-                             f"of {ng} groups; row-parallel sharding would split them")
+            # super-groups span row boundaries, so a column cut splits them: the
+            # shard keeps the fp16 scale/min the reference stores for a
+            # double-quantized tensor (codec.py:644-652, the rounded
+            # reconstruction) instead of the codes and metadata
+            s32, m32 = ql._scale_gmin_f32()
+            keep = (ql.outlier_col >= c0) & (ql.outlier_col < c1)
+            orow, ocol, odelta = _outlier_subset(ql, keep, 0, c0)
+            return _make(ql, rows=ql.rows, cols=c1 - c0, padded_cols=ngs * gs, packed=ql.packed[:, b0:b1],
+                         scale=s32[:, g0:g1].to(torch.float16), gmin=m32[:, g0:g1].to(torch.float16), dq=None,
+                         dq_group_size=0, orow=orow, ocol=ocol, odelta=odelta, bias=None)
         rows_per_sup = gsz // ng
         dq_gs = rows_per_sup * ngs
         n_sup = ql.dq_scale_meta.shape[0]
@@ -237,3 +245,42 @@ def tensor_parallelize(model: nn.Module, group=None, column_names: Sequence[str]
         elif leaf in row_names:
             _set_module_by_name(model, name, RowParallelQuantLinear(mod, group))
     return model
+
+
+def concat_rows(parts: Sequence[QuantLinear]) -> QuantLinear:
+    """One QuantLinear whose output rows are those of `parts` in order (the
+    inverse of shard_rows): e.g. q/k/v or gate/up projections fused into one
+    launch. The parts must share bits, group size, columns and codebook;
+    nothing is re-quantized, so every row reconstructs exactly as before.
+    Double-quant parts must each hold whole super-groups."""
+    p0 = parts[0]
+    for p in parts[1:]:
+        if (p.bits, p.group_size, p.cols, p.padded_cols, p.double_quant, p.dq_group_size, p.companded) != \
+                (p0.bits, p0.group_size, p0.cols, p0.padded_cols, p0.double_quant, p0.dq_group_size, p0.companded):
+            raise ValueError("concat_rows needs parts with the same layout")
+        if p.companded and not torch.equal(p.codebook, p0.codebook):
+            raise ValueError("concat_rows needs parts with the same codebook")
+    rows = sum(p.rows for p in parts)
+    offs = np.cumsum([0] + [p.rows for p in parts])
+    dq = None
+    if p0.double_quant:
+        gsz, ng = p0.dq_group_size, p0.n_groups
+        if any((p.rows * ng) % gsz for p in parts[:-1]):
+            raise ValueError("double-quant super-groups straddle the parts; concat_rows cannot keep them")
+        dq = tuple(torch.cat([getattr(p, n)[: (p.rows * ng + gsz - 1) // gsz * gsz if "codes" in n else None]
+                              for p in parts]).contiguous()
+                   for n in ("dq_scale_codes", "dq_scale_meta", "dq_gmin_codes", "dq_gmin_meta"))
+    orow = torch.cat([p.outlier_row + int(o) for p, o in zip(parts, offs[:-1])]).to(torch.int32)
+    ocol = torch.cat([p.outlier_col for p in parts]).to(torch.int32)
+    odelta = torch.cat([p.outlier_delta for p in parts])
+    bias = None
+    if any(p.bias is not None for p in parts):
+        bdt = next(p.bias.dtype for p in parts if p.bias is not None)
+        bias = torch.cat([p.bias if p.bias is not None else torch.zeros(p.rows, dtype=bdt, device=p0.packed.device)
+                          for p in parts])
+    return _make(p0, rows=rows, cols=p0.cols, padded_cols=p0.padded_cols,
+                 packed=torch.cat([p.packed for p in parts]),
+                 scale=None if dq else torch.cat([p.scale for p in parts]),
+                 gmin=None if dq else torch.cat([p.gmin for p in parts]), dq=dq,
+                 dq_group_size=p0.dq_group_size, orow=orow.contiguous(), ocol=ocol.contiguous(),
+                 odelta=odelta.contiguous(), bias=bias)

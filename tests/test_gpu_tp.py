@@ -128,7 +128,7 @@ def test_two_nccl_ranks():
         assert max(errs) <= TOL, (rank, errs)
 
 
-def _decoder_worker(rank, world, port, q):
+def _decoder_worker(rank, world, port, q, use_exchange=False):
     """Each rank builds the tensor-parallel decoder (whole layers quantized
     identically everywhere, then cut) and an unsharded copy in a one-rank
     group; the last-position logits after a prefill, and the tokens of a few
@@ -142,7 +142,11 @@ def _decoder_worker(rank, world, port, q):
         solo = [dist.new_group([r]) for r in range(world)][rank]
         cfg = DecoderConfig(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=4, intermediate=2048, vocab=4000,
                             layer_bits=[4, 8], seed=11)
-        tp_model = QuantDecoder(cfg, "cuda", max_batch=2, max_seq=64)
+        ex = None
+        if use_exchange:
+            from tensorshrink_b200.comm import PeerExchange
+            ex = PeerExchange(max_floats=1 << 16)
+        tp_model = QuantDecoder(cfg, "cuda", exchange=ex, max_batch=2, max_seq=64)
         ref_model = QuantDecoder(cfg, "cuda", group=solo, max_batch=2, max_seq=64)
         g = torch.Generator(device="cuda").manual_seed(4)
         tokens = torch.randint(0, cfg.vocab, (2, 10), device="cuda", generator=g)
@@ -166,14 +170,15 @@ def _decoder_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("use_exchange", [False, True])
 @pytest.mark.parametrize("world", [2, 4])
-def test_tensor_parallel_decoder(world):
+def test_tensor_parallel_decoder(world, use_exchange):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_decoder_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_decoder_worker, args=(r, world, port, q, use_exchange)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in procs]
@@ -184,3 +189,82 @@ def test_tensor_parallel_decoder(world):
         logit_err, disagree = vals
         assert logit_err <= 2e-2, (rank, logit_err)
         assert disagree <= 0.25, (rank, disagree)
+
+
+def _exchange_worker(rank, world, port, q):
+    """The one-shot NVLink all-reduce: exact against the rank-ordered sum of
+    all_gather'ed partials, close to NCCL's all_reduce, correct when replayed
+    from a CUDA graph, and a peer that never arrives ends a bounded wait with
+    the error flag set instead of a hang."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+        from tensorshrink_b200.comm import PeerExchange
+        import tensorshrink_b200._C as _C
+        ex = PeerExchange(max_floats=1 << 16)
+        errs = []
+        for n in (1, 4096, 5000, 65536):
+            g = torch.Generator(device="cuda").manual_seed(100 * n + rank)
+            x = torch.randn(n, device="cuda", generator=g)
+            res = torch.randn(n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(n))
+            y = ex.all_reduce(x, residual=res)
+            parts = [torch.empty_like(x) for _ in range(world)]
+            dist.all_gather(parts, x)
+            ref = parts[0].clone()
+            for p in parts[1:]:
+                ref += p
+            ref = res + ref
+            errs.append(float((y - ref).abs().max()))
+            nc = x.clone()
+            dist.all_reduce(nc)
+            errs.append(float((y - res - nc).abs().max()) * 1e-3)   # different summation order
+        # graph replay: epochs advance on the device
+        sx = torch.zeros(4096, device="cuda")
+        sy = torch.empty_like(sx)
+        ex.all_reduce(sx, out=sy)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ex.all_reduce(sx, out=sy)
+        for it in range(3):
+            sx.fill_(float(rank + 1 + it))
+            graph.replay()
+            torch.cuda.synchronize()
+            want = sum(float(r + 1 + it) for r in range(world))
+            errs.append(float((sy - want).abs().max()))
+        ex.check()
+        # a peer that never arrives: rank 0 calls alone with a 1 ms limit
+        dist.barrier()
+        timed_out = True
+        if rank == 0:
+            assert _C.load().ts_test_inject_stall(1_000_000) == 0
+            ex.all_reduce(torch.ones(64, device="cuda"))
+            torch.cuda.synchronize()
+            try:
+                ex.check()
+                timed_out = False
+            except RuntimeError:
+                timed_out = True
+        q.put((rank, errs + [0.0 if timed_out else 1.0], None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs, err in res:
+        assert err is None, (rank, err)
+        assert max(errs) == 0.0 or max(errs) < 1e-6, (rank, errs)

@@ -106,3 +106,17 @@ def test_budget_allocator():
     assert budget_allocate_bits(stats, 300) == {"a": 8, "b": 4}
     assert budget_allocate_bits(stats, 200) == {"a": 4, "b": 4}
     assert budget_allocate_bits(stats, 1000) == {"a": 8, "b": 8}
+
+
+def test_hf_config_registered_and_round_trips():
+    from transformers.quantizers.auto import AutoHfQuantizer
+    from tensorshrink_b200.hf_integration import TensorShrinkConfig
+    c = TensorShrinkConfig(bits=8, adaptive=True, modules_to_not_convert=["lm_head"])
+    assert AutoHfQuantizer.supports_quant_method(c.to_dict())
+    back = TensorShrinkConfig.from_dict(c.to_dict())
+    assert back.to_dict() == c.to_dict()
+    assert type(AutoHfQuantizer.from_config(c)).__name__ == "TensorShrinkHfQuantizer"
+    with pytest.raises(ValueError):
+        TensorShrinkConfig(bits=6)
+    with pytest.raises(NotImplementedError):
+        TensorShrinkConfig(vram_budget_mb=100)

@@ -111,3 +111,24 @@ def test_lloyd_fit_unsampled_case(golden, name):
 def test_lloyd_fit(golden, levels):
     cent = goap.lloyd_fit(golden["lloyd/sample"], levels)
     np.testing.assert_array_equal(cent, golden[f"lloyd/cent{levels}"])
+
+
+def test_oracle_smooth_and_rvq_match_reference():
+    """The oracle's smoothing and 6-bit RVQ against the reference's outputs."""
+    from pathlib import Path
+    z = np.load(Path(__file__).resolve().parent / "golden" / "golden_rvq.npz")
+    for name in z["cases"]:
+        p = f"{name}/"
+        bits, gs, dq, sm, nf = (int(v) for v in z[p + "params"])
+        q = goap.quantize(z[p + "w"], bits=bits, group_size=gs, outlier_frac=float(z[p + "frac"]),
+                          double_quant=bool(dq), mode="nf" if nf else "uniform", smooth=bool(sm),
+                          smooth_alpha=float(z[p + "alpha"]))
+        for f in ("packed", "scale", "gmin", "smooth_scale", "stage2_packed", "stage2_scale", "stage2_gmin",
+                  "dq_scale_codes", "dq_gmin_meta"):
+            if p + f in z.files:
+                np.testing.assert_array_equal(getattr(q, f).view(np.uint8), z[p + f].view(np.uint8),
+                                              err_msg=f"{name} {f}")
+        W, ref = goap.dequantize(q), z[p + "W"]
+        tied = ~np.isin(q.outlier_idx, z[p + "outlier_idx"])
+        assert tied.sum() <= 2, name
+        np.testing.assert_allclose(W, ref, rtol=0, atol=1e-3 * np.abs(ref).max())

@@ -79,12 +79,13 @@ def test_row_shards_reconstruct_column_slices(golden, name, world):
         except ValueError:
             pytest.skip("groups do not split evenly")
         c1 = min(c1, ql.cols)
-        try:
-            sh = tp.shard_cols(ql, c0, c1)
-        except ValueError as e:
-            assert ql.double_quant and "super-groups" in str(e)
-            return
-        np.testing.assert_array_equal(dense(sh), W[:, c0:c1])
+        sh = tp.shard_cols(ql, c0, c1)
+        if ql.double_quant and not sh.double_quant:
+            # super-groups straddle the cut: the shard keeps the fp16-rounded
+            # scale/min (what the reference stores for a double-quantized tensor)
+            np.testing.assert_allclose(dense(sh), W[:, c0:c1], rtol=0, atol=2e-3 * np.abs(W).max())
+        else:
+            np.testing.assert_array_equal(dense(sh), W[:, c0:c1])
         assert sh.bias is None
     del cols
 
