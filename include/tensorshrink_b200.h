@@ -102,6 +102,22 @@ TS_API int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M
                size_t workspace_bytes, void* stream);
 
 /*
+ * Gated MLP projection: out = (silu(gate) * up) . W^T (+ outliers)(+ bias),
+ * with gate_up [M, 2 * cols] holding gate in columns [0, cols) and up in
+ * [cols, 2 cols) (the output of a fused gate/up projection). silu(gate) and
+ * the product are rounded to x_dtype as the unfused F.silu(gate) * up
+ * rounds them. Decode-sized calls only (the decode kernel computes the
+ * product while staging the activations): TS_ERR_UNSUPPORTED otherwise,
+ * and the caller runs the product and ts_qlinear. Replaces the
+ * `F.silu(gate) * up` elementwise pass in front of the reference's down
+ * projection (the reference has no fused form). Workspace as ts_qlinear.
+ */
+TS_API int ts_qlinear_gated(const ts_qweight* w, const void* gate_up, int x_dtype, int64_t M,
+               int64_t x_row_stride, const void* bias, int bias_dtype, void* out,
+               int out_dtype, int64_t out_row_stride, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/*
  * Allocation-free variant of ts_qlinear (no counterpart in the reference):
  * same arguments minus the workspace. The decode kernel's scratch lives in a
  * fixed per-device array of ts_qlinear_noalloc_max_scratch() bytes (512 KiB)

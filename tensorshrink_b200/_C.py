@@ -71,6 +71,8 @@ _SIGNATURES = [
     ("ts_qlinear_workspace_size", C.c_size_t, [C.POINTER(TsQWeight), _i64]),
     ("ts_qlinear", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int, _vp,
                              C.c_int, _i64, _vp, C.c_size_t, _vp]),
+    ("ts_qlinear_gated", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int, _vp,
+                                   C.c_int, _i64, _vp, C.c_size_t, _vp]),
     ("ts_qlinear_noalloc_max_scratch", C.c_size_t, []),
     ("ts_qlinear_noalloc", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int,
                                      _vp, C.c_int, _i64, _vp]),
@@ -133,6 +135,25 @@ def check(rc: int, what: str) -> None:
     if rc != 0:
         msg = load().ts_last_error().decode(errors="replace")
         raise _STATUS.get(rc, RuntimeError)(f"{what}: {msg}")
+
+
+_TORCH_LIB_PATH = _LIB_PATH.parent / "libtensorshrink_torch.so"
+_ops = None
+
+
+def torch_ops():
+    """The `torch.ops.tensorshrink` namespace (operators over this library,
+    built beside it), loaded once; None when that library was not built."""
+    global _ops
+    if _ops is None:
+        load()
+        if not _TORCH_LIB_PATH.exists():
+            _ops = False
+        else:
+            import torch
+            torch.ops.load_library(str(_TORCH_LIB_PATH))
+            _ops = torch.ops.tensorshrink
+    return _ops or None
 
 
 def launch_count(reset: bool = False) -> int:

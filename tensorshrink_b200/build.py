@@ -28,6 +28,8 @@ INCLUDE = ROOT / "include"
 LIBDIR = PKG / "_lib"
 OBJDIR = PKG / "_lib" / "obj"
 LIBNAME = "libtensorshrink_b200.so"
+TORCH_LIBNAME = "libtensorshrink_torch.so"
+TORCH_SRC = PKG / "csrc_torch" / "ops.cpp"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
@@ -94,7 +96,31 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_torch_ops(lib, verbose)
     return lib
+
+
+def build_torch_ops(lib: Path, verbose: bool = False) -> Path:
+    """`libtensorshrink_torch.so`: the torch.ops.tensorshrink operators, a
+    thin C++ layer (host code only) over the C ABI library."""
+    import torch.utils.cpp_extension as ce
+    out = LIBDIR / TORCH_LIBNAME
+    deps = [TORCH_SRC, lib] + list(INCLUDE.glob("*.h"))
+    if out.exists() and out.stat().st_mtime >= max(f.stat().st_mtime for f in deps):
+        return out
+    import torch
+    cuda_inc = Path(nvcc()).resolve().parent.parent / "include"
+    cmd = ["g++", "-O2", "-shared", "-fPIC", "-std=c++17", str(TORCH_SRC), "-o", str(out),
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           *[f"-I{p}" for p in ce.include_paths()], f"-I{cuda_inc}", f"-I{INCLUDE}",
+           *[f"-L{p}" for p in ce.library_paths()], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_cuda", f"-L{LIBDIR}", "-ltensorshrink_b200", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch ops build failed:\n{r.stdout}\n{r.stderr}")
+    return out
 
 
 if __name__ == "__main__":

@@ -69,18 +69,28 @@ __global__ void __launch_bounds__(kThreads) oneshot_kernel(const Args a) {
   __syncthreads();
   const uint32_t e = s_epoch;
   const int p = e & 1;
-  const int64_t chunk = (a.n + gridDim.x - 1) / gridDim.x;
+  const int64_t chunk = ((a.n + gridDim.x - 1) / gridDim.x + 3) & ~(int64_t)3;
   const int64_t c0 = blockIdx.x * chunk, c1 = min(a.n, c0 + chunk);
 
-  // 1. push this rank's chunk to every rank (float4 when aligned)
+  // 1. push this rank's chunk to every rank (16-byte stores; chunks are
+  //    multiples of 4 floats and the slots 16-byte aligned)
+  const bool vec = ((reinterpret_cast<uintptr_t>(a.in) & 15) == 0) && (a.cap % 4 == 0);
   for (int r = 0; r < a.world; ++r) {
     float* dst = a.peer_buf[r] + ((int64_t)p * a.world + a.rank) * a.cap;
-    for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) dst[i] = a.in[i];
+    if (vec) {
+      const int64_t v1 = c1 & ~(int64_t)3;
+      for (int64_t i = c0 + 4 * threadIdx.x; i < v1; i += 4 * blockDim.x)
+        *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(a.in + i);
+      for (int64_t i = v1 + threadIdx.x; i < c1; i += blockDim.x) dst[i] = a.in[i];
+    } else {
+      for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) dst[i] = a.in[i];
+    }
   }
-  // 2. publish
-  __threadfence_system();
+  // 2. publish: the block's stores are ordered before one system-scope
+  //    fence by the threads that write the flags
   __syncthreads();
   if (threadIdx.x < a.world) {
+    __threadfence_system();
     uint32_t* f = flags_of(a.peer_buf[threadIdx.x], a.cap, a.world) + ((int64_t)p * a.world + a.rank) * kMaxBlocks +
                   blockIdx.x;
     st_release_sys(f, e);

@@ -20,7 +20,7 @@ namespace ts {
   int gemv_max_tokens(const ts_qweight& w);                                                          \
   int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,        \
                const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,      \
-               void* workspace, size_t ws_bytes, cudaStream_t stream);                               \
+               void* workspace, size_t ws_bytes, cudaStream_t stream, int gated);                    \
   }
 TS_DECLARE_GEMV(gemv_v1)
 TS_DECLARE_GEMV(gemv_v2)
@@ -37,13 +37,13 @@ static size_t gemv_workspace_size(const ts_qweight& w) {
 // workspace covers it; one CTA per SM otherwise.
 static int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
                     const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
-                    void* workspace, size_t ws_bytes, cudaStream_t stream) {
+                    void* workspace, size_t ws_bytes, cudaStream_t stream, int gated = 0) {
   if (gemv_v2::gemv_supported(w) && M <= gemv_v2::gemv_max_tokens(w) &&
       ws_bytes >= gemv_v2::gemv_workspace_size(w))
     return gemv_v2::run_gemv(w, x, x_dtype, M, x_stride, bias, bias_dtype, out, out_dtype, out_stride,
-                             workspace, ws_bytes, stream);
+                             workspace, ws_bytes, stream, gated);
   return gemv_v1::run_gemv(w, x, x_dtype, M, x_stride, bias, bias_dtype, out, out_dtype, out_stride,
-                           workspace, ws_bytes, stream);
+                           workspace, ws_bytes, stream, gated);
 }
 int run_generic_qlinear(const ts_qweight& w, const void* x, int x_dtype, int64_t M,
                         int64_t x_stride, const void* bias, int bias_dtype, void* out,
@@ -218,6 +218,24 @@ int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M, int64
   }
   return run_generic_qlinear(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
                              out_row_stride, s);
+}
+
+int ts_qlinear_gated(const ts_qweight* w, const void* gate_up, int x_dtype, int64_t M, int64_t x_row_stride,
+                     const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_row_stride,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_qweight(w);
+  if (rc != TS_OK) return rc;
+  TS_UNSUPPORTED(valid_act_dtype(x_dtype), "x dtype must be fp16 or bf16");
+  TS_UNSUPPORTED(valid_dtype(out_dtype), "out dtype must be fp16, bf16 or fp32");
+  TS_REQUIRE(M >= 0, "M < 0");
+  if (M == 0 || w->rows == 0) return TS_OK;
+  TS_REQUIRE(gate_up != nullptr && out != nullptr && workspace != nullptr, "NULL pointer");
+  TS_REQUIRE(x_row_stride >= 2 * w->cols && out_row_stride >= w->rows, "row strides too small");
+  TS_REQUIRE(w->n_outliers == 0 || w->outlier_row_ptr != nullptr, "qlinear needs the CSR outlier_row_ptr table");
+  TS_UNSUPPORTED(gemv_supported(*w) && M <= gemv_v1::gemv_max_tokens(*w),
+                 "gated qlinear runs in the decode kernel only (M=%lld)", (long long)M);
+  return run_gemv(*w, gate_up, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride,
+                  workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), 1);
 }
 
 int ts_apply_outlier_correction(float* out, int64_t M, int64_t N, int64_t out_row_stride,

@@ -96,6 +96,10 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));  // (a & b) | c
   return r;
 }
+// fp32 -> the activation dtype -> fp32 (round to nearest even)
+__device__ __forceinline__ float round_act(float v, int dtype) {
+  return dtype == TS_F16 ? __half2float(__float2half_rn(v)) : __bfloat162float(__float2bfloat16_rn(v));
+}
 __device__ __forceinline__ half2 u2h2(uint32_t v) { return *reinterpret_cast<half2*>(&v); }
 __device__ __forceinline__ uint32_t h22u(half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ uint32_t hsub(uint32_t a, uint32_t b) { return h22u(__hsub2(u2h2(a), u2h2(b))); }
@@ -178,6 +182,7 @@ struct Args {
   int* err;            // wait-timeout flag (read back by ts_qlinear_status)
   uint64_t wait_ns;    // limit of every barrier wait
   int stall;           // test hook: the producer issues no copies, so the first waits run out
+  int gated;           // x rows hold [gate | up] (2 * cols): the input is silu(gate) * up
   uint32_t tiles;      // row_blocks * kgroups
   uint32_t kgroups;    // tiles per row block
   uint32_t grid;
@@ -428,25 +433,41 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       const uint32_t k0 = live ? (it - n * per_tok) * 16 : 0;
       const int64_t xo = (a.m0 + n) * a.x_stride + k0;
       float v[16];
-      if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
-        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + xo);
-        const uint4 r0 = __ldg(p), r1 = __ldg(p + 1);
-        const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+      // 16 activations at element offset `off` of the token's row
+      auto load16 = [&](int64_t off, float (&o)[16]) {
+        if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
+          const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + off);
+          const uint4 r0 = __ldg(p), r1 = __ldg(p + 1);
+          const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (a.x_dtype == TS_F16) {
-            const float2 f = __half22float2(u2h2(rw[j]));
-            v[2 * j] = f.x;
-            v[2 * j + 1] = f.y;
-          } else {
-            v[2 * j] = __uint_as_float(rw[j] << 16);
-            v[2 * j + 1] = __uint_as_float(rw[j] & 0xFFFF0000u);
+          for (int j = 0; j < 8; ++j) {
+            if (a.x_dtype == TS_F16) {
+              const float2 f = __half22float2(u2h2(rw[j]));
+              o[2 * j] = f.x;
+              o[2 * j + 1] = f.y;
+            } else {
+              o[2 * j] = __uint_as_float(rw[j] << 16);
+              o[2 * j + 1] = __uint_as_float(rw[j] & 0xFFFF0000u);
+            }
           }
-        }
-      } else {
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          v[j] = (live && k0 + j < (uint32_t)a.q.cols) ? load_f(a.x, a.x_dtype, xo + j) : 0.f;
+          for (int j = 0; j < 16; ++j)
+            o[j] = (live && k0 + j < (uint32_t)a.q.cols) ? load_f(a.x, a.x_dtype, off + j) : 0.f;
+        }
+      };
+      load16(xo, v);
+      if (a.gated) {
+        // gated MLP input: x = silu(gate) * up with gate, up the two halves of
+        // the row, each rounded to the activation dtype as the unfused
+        // F.silu(gate) * up would round them
+        float u[16];
+        load16(xo + a.q.cols, u);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float sl = round_act(v[j] / (1.f + __expf(-v[j])), a.x_dtype);
+          v[j] = round_act(sl * u[j], a.x_dtype);
+        }
       }
       float mx = 0.f, sum = 0.f;
 #pragma unroll
@@ -1120,7 +1141,7 @@ int gemv_max_tokens(const ts_qweight& w) {
 
 int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
              const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
-             void* workspace, size_t ws_bytes, cudaStream_t stream) {
+             void* workspace, size_t ws_bytes, cudaStream_t stream, int gated) {
   const int max_mt = gemv_max_tokens(w);
   TS_UNSUPPORTED(max_mt > 0, "qlinear: activations of %lld columns do not fit in shared memory",
                  (long long)w.cols);
@@ -1142,6 +1163,7 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.err = reinterpret_cast<int*>(ws + gemv_partials_bytes());
   a.wait_ns = wait_limit_ns();
   a.stall = take_test_stall() ? 1 : 0;
+  a.gated = gated;
   a.counters = reinterpret_cast<int*>(ws + gemv_partials_bytes() + 256);
   a.tiles = p.tiles;
   a.kgroups = p.kgroups;
@@ -1157,7 +1179,7 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.dq_shift = -1;
   if (w.dq_group_size > 0 && (w.dq_group_size & (w.dq_group_size - 1)) == 0) a.dq_shift = ilog2(w.dq_group_size);
   const bool dq = w.dq_scale_codes != nullptr;
-  a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0;
+  a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0 && (!gated || (w.cols * 2) % 16 == 0);
   a.meta_bulk = p.meta_bulk ? 1 : 0;
   if (p.meta_bulk) {
     const CUtensorMapDataType t = dq ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;

@@ -131,6 +131,18 @@ class ShardedProjection(nn.Module):
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
+def _gated(self, gate_up: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """This layer applied to silu(gate) * up, gate_up = [gate | up] (the
+    output of the fused gate/up projection): one fused launch at decode."""
+    from . import kernels
+    g2d = gate_up.reshape(-1, gate_up.shape[-1])
+    y = kernels.qlinear_gated(g2d, self.local.qweight(), self.local.bias, out_dtype or gate_up.dtype)
+    return y.reshape(*gate_up.shape[:-1], y.shape[-1])
+
+
+ShardedProjection.gated = _gated
+
+
 class FusedProjection(nn.Module):
     """A QuantLinear called through kernels.qlinear (rows of several
     projections)."""
@@ -278,8 +290,8 @@ class QuantDecoder(nn.Module):
         a = a.transpose(1, 2).reshape(B, T, layer.n_heads_local * D)
         h = self._reduce_add(layer.o_proj(a, torch.float32), h)
         x = _rms_norm(h, layer.post_norm, cfg.rms_eps)
-        g, u = layer.gate_up(x).split([layer.split_gate, layer.split_gate], dim=-1)
-        return self._reduce_add(layer.down_proj(F.silu(g) * u, torch.float32), h)
+        gu = layer.gate_up(x)
+        return self._reduce_add(layer.down_proj.gated(gu, torch.float32), h)
 
     def _next_token(self, h_last: torch.Tensor) -> torch.Tensor:
         """Greedy next token: global argmax over the vocabulary shards."""

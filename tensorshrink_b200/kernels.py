@@ -174,6 +174,12 @@ def device_status(device: Optional[torch.device] = None, clear: bool = True) -> 
     lib = _C.load()
     with torch.cuda.device(dev):
         stream = _stream_handle(dev)
+        ops = _C.torch_ops()
+        if ops is not None:       # the workspaces of torch.ops.tensorshrink.qlinear
+            try:
+                ops.device_status(dev.index, clear)
+            except RuntimeError as e:
+                raise RuntimeError(f"ts_qlinear_status: {e}") from None
         bufs = _WORKSPACES.on_device(dev.index) + [None]   # None: the no-alloc scratch
         for b in bufs:
             if b is None:
@@ -208,6 +214,33 @@ def qlinear(x2d: torch.Tensor, qw: _C.TsQWeight, bias: Optional[torch.Tensor], o
                         out.data_ptr(), dtype_code(out.dtype), int(out.stride(0)),
                         workspace.data_ptr(), int(workspace.numel()), _stream_handle(x2d.device))
     _C.check(rc, "ts_qlinear")
+    return out
+
+
+def qlinear_gated(gate_up: torch.Tensor, qw: _C.TsQWeight, bias: Optional[torch.Tensor], out_dtype: torch.dtype,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, rows] = (silu(gate) * up) @ W^T for gate_up = [gate | up]
+    ([M, 2 * cols], e.g. a fused gate/up projection's output): one
+    `ts_qlinear_gated` launch for decode-sized M (the product is formed while
+    the kernel stages its activations); F.silu(gate) * up then `ts_qlinear`
+    for larger M."""
+    lib = _C.load()
+    M, K = int(gate_up.shape[0]), int(qw.cols)
+    if gate_up.stride(-1) != 1:
+        gate_up = gate_up.contiguous()
+    if out is None:
+        out = torch.empty((M, qw.rows), dtype=out_dtype, device=gate_up.device)
+    if M == 0:
+        return out
+    workspace = workspace_for(gate_up.device, int(lib.ts_qlinear_workspace_size(qw, M)))
+    rc = lib.ts_qlinear_gated(qw, gate_up.data_ptr(), dtype_code(gate_up.dtype), M, int(gate_up.stride(0)),
+                              _ptr(bias), dtype_code(bias.dtype) if bias is not None else 0,
+                              out.data_ptr(), dtype_code(out.dtype), int(out.stride(0)),
+                              workspace.data_ptr(), int(workspace.numel()), _stream_handle(gate_up.device))
+    if rc == -2:    # not a decode-sized call: the elementwise product, then the GEMM
+        g, u = gate_up[:, :K], gate_up[:, K:2 * K]
+        return qlinear((torch.nn.functional.silu(g) * u).contiguous(), qw, bias, out_dtype, out=out)
+    _C.check(rc, "ts_qlinear_gated")
     return out
 
 

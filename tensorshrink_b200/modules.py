@@ -28,7 +28,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import kernels
+from . import _C, kernels
 from .codec import (
     DEFAULT_DQ_GROUP_SIZE,
     DeviceQuant,
@@ -384,6 +384,17 @@ class QuantLinear(nn.Module):
         in_dtype = x.dtype
         compute_dtype = torch.float32 if self.force_fp32_compute else in_dtype
         if compute_dtype in (torch.float16, torch.bfloat16):
+            ops = _C.torch_ops()
+            if ops is not None:
+                # one dispatcher call: torch.ops.tensorshrink.qlinear over ts_qlinear
+                dq = self.double_quant
+                return ops.qlinear(
+                    x, self.packed, self.scale, self.gmin,
+                    self.dq_scale_codes if dq else None, self.dq_scale_meta if dq else None,
+                    self.dq_gmin_codes if dq else None, self.dq_gmin_meta if dq else None,
+                    self.codebook if self.companded else None, self.outlier_row_ptr, self.outlier_col,
+                    self.outlier_delta, self.bias, self.bits, self.group_size, self.cols, self.out_features,
+                    self.n_groups, self.dq_group_size, compute_dtype)
             x2d = x.reshape(-1, self.in_features)
             if not x2d.is_contiguous():
                 x2d = x2d.contiguous()
