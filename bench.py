@@ -25,8 +25,11 @@ bf16 on the tensor-core kernel, each launch timed alone after an L2 flush,
 and a `quantize` object: fp16-input GB/s of the GPU quantize/pack on the
 BASELINE configs[4] [28672, 8192] shape (4-bit g128, double quant).
 
---impl reference times the reference algorithm's CPU path (the numpy port
-in oracle/, on all host threads) on a bounded sample of the same workload.
+--impl reference times the unmodified reference (installed into baseline/_ref
+by baseline/install_ref.py): its QuantLinear.forward CPU path on one full MLP
+block on all host threads as `value`, and, on a GPU host, its own CUDA/Triton
+path on the same blocks as `gpu_anchor`. Without the install it falls back to
+the oracle's numpy port of the CPU path.
 """
 
 from __future__ import annotations
@@ -704,17 +707,119 @@ def cpu_baseline(blocks, M, budget_s=10.0, impl_steps=None):
 
 
 # ---------------------------------------------------------------------------
-# reference arm (CPU port of the reference path)
+# reference arm: the unmodified reference (baseline/_ref), else the oracle port
 # ---------------------------------------------------------------------------
 
-def run_reference(args, rank, world):
-    if rank != 0:
+REF_DIR = ROOT / "baseline" / "_ref" / "tensorshrink"
+
+
+def load_reference_modules():
+    """The reference's `tensorshrink.modules`, imported from baseline/_ref
+    (placed there unchanged by baseline/install_ref.py). The package
+    `__init__` needs `zstandard` (absent), so the submodules are imported
+    under a bare package object; None when the install is missing."""
+    if not (REF_DIR / "modules.py").exists():
         return None
+    import importlib
+    import types
+    pkg = types.ModuleType("tensorshrink")
+    pkg.__path__ = [str(REF_DIR)]
+    sys.modules["tensorshrink"] = pkg
+    return importlib.import_module("tensorshrink.modules")
+
+
+def student_t_torch(shape, seed, device):
+    """The bench's weight distribution (Student-t df=4, std 0.02, fp16),
+    drawn with a seeded generator on `device`."""
+    if str(device).startswith("cuda"):
+        return student_t_cuda(shape, seed, device)
     import torch
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(shape, generator=g)
+    chi = torch.zeros(shape)
+    for _ in range(4):
+        chi += torch.randn(shape, generator=g).square()
+    w = z / torch.sqrt(chi / 4.0)
+    w *= 0.02 / w.std()
+    return w.to(torch.float16)
+
+
+def reference_block(refmod, device, seed0=0, rows_frac=1.0):
+    """One MLP block (gate, up, down) as the reference's QuantLinear, built
+    by its own `QuantLinear.from_linear` with the bench's settings (4-bit
+    g128 uniform, 0.1% outliers, no double quant). `rows_frac` < 1 keeps
+    that leading fraction of each weight's rows (a bounded sample)."""
+    import torch
+    layers = []
+    for j, shape in enumerate(((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER))):
+        rows = max(128, int(shape[0] * rows_frac) // 128 * 128)
+        w = student_t_torch(shape, seed0 + j, device)[:rows]
+        lin = torch.nn.Linear(shape[1], rows, bias=False, device=device, dtype=torch.float16)
+        with torch.no_grad():
+            lin.weight.copy_(w)
+        q, _, _ = refmod.QuantLinear.from_linear(lin, bits=4, group_size=128, outlier_frac=0.001,
+                                                 double_quant=False, nf_quant=False)
+        layers.append(q)
+        del w, lin
+    return layers
+
+
+def reference_mlp(block, x):
+    """gate/up/down through the reference modules, SiLU-gated like the
+    library's fused path."""
+    import torch.nn.functional as F
+    gate, up, down = block
+    return down(F.silu(gate(x)) * up(x))
+
+
+def reference_step_bytes(blocks, M):
+    return sum(q.packed_nbytes() + 2 * M * (q.in_features + q.out_features) for b in blocks for q in b)
+
+
+def reference_gpu_anchor(refmod, args):
+    """The reference's own CUDA path (QuantLinear.forward -> Triton
+    `fused_quantized_linear` for M <= 64) on cuda:0: the same blocks, M and
+    step as the library's device-timed `value`, timed with CUDA events."""
+    import torch
+    try:
+        import triton
+        tver = triton.__version__
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"triton not importable: {e}"}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    blocks = [reference_block(refmod, dev, seed0=10 * b) for b in range(args.blocks)]
+    x0 = torch.randn(args.M, HIDDEN, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        x = x0
+        for blk in blocks:
+            x = reference_mlp(blk, x)
+        return x
+
+    with torch.no_grad():
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = reference_step_bytes(blocks, args.M)
+    used_triton = all(getattr(q, "_triton_eligible", False) for b in blocks for q in b)
+    return {"value": round(nbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "path": "reference QuantLinear.forward on cuda:0, eager"
+                    + (" (Triton fused_quantized_linear)" if used_triton else " (no Triton path)"),
+            "triton": tver, "blocks": args.blocks, "bytes_per_step": nbytes}
+
+
+def run_reference_port(args, world, threads):
+    """Fallback when baseline/_ref is not installed: the oracle's numpy
+    restatement of the reference's CPU path on a 512-row sample."""
     from oracle import goap
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    # the same synthetic block, quantized by the numpy port (fp16 weights)
     rng = np.random.default_rng(0)
     qts = []
     rows_per_step = 512
@@ -738,20 +843,73 @@ def run_reference(args, rank, world):
     for _ in range(args.steps):
         step()
     dt = (time.perf_counter() - t0) / args.steps
-    value = bytes_step / dt / 1e9
     sample = (f"{rows_per_step} rows of each of gate/up/down ([14336,4096] x2, [4096,14336]) at "
-              f"M={args.M}: numpy dequant + matmul in 128-row chunks on {threads} threads")
-    return {
+              f"M={args.M}: oracle numpy port, 128-row chunks on {threads} threads")
+    return bytes_step / dt / 1e9, dt, "port", sample, {"sample_rows_per_matrix": rows_per_step}
+
+
+def run_reference_unmodified(args, refmod, threads):
+    """The reference's QuantLinear.forward on CPU tensors (its chunked
+    `_dequantize_rows` + F.linear path, modules.py:924-940) over one full
+    config-2 MLP block, bf16 activations, all host threads. If (K + W)
+    full steps would pass ~150 s, each weight keeps a leading row sample."""
+    import torch
+    budget_s = 150.0
+    block = reference_block(refmod, "cpu")
+    x = torch.randn(args.M, HIDDEN, dtype=torch.bfloat16)
+    with torch.no_grad():
+        reference_mlp(block, x)
+        t0 = time.perf_counter()
+        reference_mlp(block, x)
+        t_full = time.perf_counter() - t0
+    frac = min(1.0, budget_s / max(1, args.steps + args.warmup) / max(t_full, 1e-6))
+    if frac < 1.0:
+        block = reference_block(refmod, "cpu", rows_frac=frac)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            reference_mlp(block, x)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            reference_mlp(block, x)
+        dt = (time.perf_counter() - t0) / args.steps
+    rows = [q.out_features for q in block]
+    nbytes = reference_step_bytes([block], args.M)
+    sample = ("one MLP block, gate/up/down rows " + str(rows)
+              + " of [14336,4096] x2 / [4096,14336]"
+              + (" (full size)" if frac >= 1.0 else f" (leading {frac:.3f} of rows)")
+              + f", M={args.M} bf16: unmodified reference QuantLinear.forward on CPU tensors, "
+              f"{threads} threads")
+    return nbytes / dt / 1e9, dt, "reference", sample, {"rows_per_matrix": rows, "same_config": frac >= 1.0}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    refmod = load_reference_modules()
+    if refmod is not None:
+        value, dt, kind, sample, extra = run_reference_unmodified(args, refmod, threads)
+    else:
+        value, dt, kind, sample, extra = run_reference_port(args, world, threads)
+    out = {
         "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes x fp32", "data": "synthetic",
-        "config": {"workload": "llama_mlp_h4096_i14336_w4g128_uniform_outlier0.001_decode", "M": args.M,
-                   "sample_rows_per_matrix": rows_per_step},
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes x bf16", "data": "synthetic",
+        "config": dict({"workload": "llama_mlp_h4096_i14336_w4g128_uniform_outlier0.001_decode", "M": args.M},
+                       **extra),
         "impl": "reference",
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if refmod is not None and torch.cuda.is_available() and not args.no_ref_gpu:
+        try:
+            out["gpu_anchor"] = reference_gpu_anchor(refmod, args)
+        except Exception as e:  # noqa: BLE001
+            out["gpu_anchor"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    return out
 
 
 def main():
@@ -769,6 +927,8 @@ def main():
     ap.add_argument("--no-decoder", action="store_true", help="skip the Llama-3-8B-shaped decoder")
     ap.add_argument("--nccl", action="store_true", help="tensor-parallel exchanges through NCCL instead of the "
                                                        "library's one-shot all-reduce kernel")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="--impl reference: skip the reference's own CUDA/Triton timing")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()
