@@ -52,6 +52,8 @@ METRIC = "QuantLinear packed-weight HBM GB/s (M=1) & TFLOP/s (M=2048); decode to
 HIDDEN, INTER = 4096, 14336
 # DRAM bytes per launch (read + write) measured by ncu on this workload
 QGEMV_TRAFFIC_BYTES = 31_679_488
+# the one-GPU step runs as one chained launch (see mlp_step)
+STEP_CHAIN = True
 QGEMM_TRAFFIC_BYTES = 57_634_816 + 12_308_736
 
 
@@ -165,13 +167,47 @@ def layer_of(p):
     return getattr(p, "local", p)
 
 
-def mlp_step(blocks, x, world=1, exchange=None):
-    """One decode step through the MLP blocks. With world > 1 the down
-    projection's fp32 partial sums are summed over the ranks by the
-    library's one-shot NVLink all-reduce (`exchange`), or NCCL without one."""
+_CHAINS = {}
+
+
+def chain_steps(blocks, x, per_block):
+    """The step as `qlinear_chain` lists: one chain of every layer (gate|up
+    then the gated down projection of each block in turn), or one chain per
+    block. Intermediate buffers are allocated once per (blocks, input)."""
+    import torch
+    from tensorshrink_b200.kernels import ChainStep
+    key = (id(blocks), x.data_ptr(), tuple(x.shape), per_block)
+    got = _CHAINS.get(key)
+    if got is None:
+        groups, cur = [[]], x
+        for gate_up, down in blocks:
+            gu = torch.empty(x.shape[0], layer_of(gate_up).rows, dtype=x.dtype, device=x.device)
+            y = torch.empty(x.shape[0], layer_of(down).rows, dtype=x.dtype, device=x.device)
+            if per_block and groups[-1]:
+                groups.append([])
+            groups[-1] += [ChainStep(layer_of(gate_up).qweight(), cur, gu),
+                           ChainStep(layer_of(down).qweight(), gu, y, gated=True)]
+            cur = y
+        got = (groups, cur)
+        _CHAINS[key] = got
+    return got
+
+
+def mlp_step(blocks, x, world=1, exchange=None, chain="step"):
+    """One decode step through the MLP blocks. On one GPU the layers run as
+    chained persistent launches (`chain`: "step" = one launch for every
+    layer, "block" = one per block, None = one launch per layer). With
+    world > 1 the down projection's fp32 partial sums are summed over the
+    ranks by the library's one-shot NVLink all-reduce (`exchange`), or NCCL
+    without one."""
     import torch
     import torch.distributed as dist
-    import torch.nn.functional as F
+    if world == 1 and chain:
+        from tensorshrink_b200.kernels import qlinear_chain
+        groups, y = chain_steps(blocks, x, chain == "block")
+        for g in groups:
+            qlinear_chain(g)
+        return y
     for gate_up, down in blocks:
         gu = gate_up(x)
         if world == 1:
@@ -542,25 +578,38 @@ def run_ours(args, rank, world, device):
         bytes_job = float(bytes_step)
     value = bytes_job / (ms_per_step * 1e-3) / 1e9
 
-    # ---- dominant kernel: the GEMV launches alone, graph-replayed ----
-    layers = [p for blk in blocks for p in blk]
-    gx = {}
-    for p in layers:
-        k = layer_of(p).in_features
-        if k not in gx:
-            gx[k] = torch.randn(M, k, device=device).to(torch.bfloat16)
-    kgraph = torch.cuda.CUDAGraph()
-    for p in layers:
-        p(gx[layer_of(p).in_features])
-    torch.cuda.synchronize(device)
-    with torch.cuda.graph(kgraph):
-        for p in layers:
-            p(gx[layer_of(p).in_features])
-    for _ in range(3):
-        kgraph.replay()
+    # ---- the step's launch structures, each graph-replayed ----
+    # unchained: one launch per layer (the per-launch GEMV roofline);
+    # per block: gate|up + gated down chained; whole step: one launch
     reps = max(args.steps, 10)
-    kms = timed(kgraph.replay, reps) / (reps * len(layers))
-    kbytes = bytes_step / len(layers)
+    variants = {}
+    for name, mode in (("per_layer", None), ("chain_per_block", "block"), ("chain_step", "step")):
+        if world > 1 and mode:
+            continue
+        vx = torch.randn(M, HIDDEN, device=device).to(torch.bfloat16)
+        for _ in range(2):
+            mlp_step(blocks, vx, world, exchange, chain=mode)
+        torch.cuda.synchronize(device)
+        _C.launch_count(reset=True)
+        vg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(vg):
+            mlp_step(blocks, vx, world, exchange, chain=mode)
+        nl = _C.launch_count(reset=True)
+        for _ in range(3):
+            vg.replay()
+        vms = timed(vg.replay, reps) / reps
+        variants[name] = {"GB/s": round(bytes_job / (vms * 1e-3) / 1e9, 1), "ms_per_step": round(vms, 5),
+                          "launches_per_step": int(nl)}
+        del vg
+    n_layers = 2 * len(blocks)
+    if world == 1 and STEP_CHAIN:
+        # the timed step is ONE persistent launch over every layer
+        kms, kbytes = ms_per_step, bytes_step
+        k_kernel = "ts::gemv_v2::gemv::qgemv_kernel<4,false,false,4,8> (chain of all layers, one launch)"
+    else:
+        kms = variants["per_layer"]["ms_per_step"] / n_layers
+        kbytes = bytes_step / n_layers
+        k_kernel = "ts::gemv_v2::gemv::qgemv_kernel<4,false,false,4,1> (gate|up and down GEMVs, one launch each)"
     k_gbs = kbytes / (kms * 1e-3) / 1e9
 
     # ---- e2e: public module API, pinned host input/output ----
@@ -604,7 +653,7 @@ def run_ours(args, rank, world, device):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(blocks, M, budget_s=args.cpu_seconds)
-    del blocks, graph, kgraph, e2e_graph
+    del blocks, graph, e2e_graph
     torch.cuda.empty_cache()
     decoder = decoder_measure(device, world, timed, exchange=exchange) if not args.no_decoder else None
     decoder70 = None
@@ -631,7 +680,10 @@ def run_ours(args, rank, world, device):
             "data": "synthetic (seeded Student-t(df=4) weights, N(0,1) activations)",
             "config": {
                 "workload": "llama_mlp_h4096_i14336_w4g128_uniform_outlier0.001_decode",
-                "M": M, "blocks": args.blocks, "matrices_per_step": 3 * args.blocks, "launches_per_block": "2 (fused gate|up GEMV, gated down GEMV)",
+                "M": M, "blocks": args.blocks, "matrices_per_step": 3 * args.blocks, "launches_per_step": int(launches_per_step),
+                "structure": ("one persistent chained launch over every layer (fused gate|up, gated down per block)"
+                              if world == 1 and STEP_CHAIN else
+                              "per block: fused gate|up GEMV, gated down GEMV (+ all-reduce)"),
                 "bytes_per_step": bytes_step,
                 "l2": f"inputs larger than L2: {args.blocks} distinct MLP blocks "
                       f"({bytes_step / 1e6:.0f} MB packed) streamed per step",
@@ -650,14 +702,14 @@ def run_ours(args, rank, world, device):
                             "result copy; K graph replays between CUDA events",
                     "eager": {"value": round(eager_val, 2), "ms_per_step": round(eager_ms, 5),
                               "path": "the same calls issued from Python every step"}},
-            "roofline": {"kernel": "ts::gemv_v2::gemv::qgemv_kernel<4,false,false,4> (gate/up), gemv_v2 or gemv_v1 (down)", "bound": "hbm",
+            "step_variants": variants,
+            "roofline": {"kernel": k_kernel, "bound": "hbm",
                          "achieved": round(k_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(k_gbs / hbm_peak, 4), "peak_kind": peak_kind,
                          "bytes_per_launch": int(kbytes), "us_per_launch": round(kms * 1e3, 3),
                          # dram__bytes_read.sum + dram__bytes_write.sum of one ncu
-                         # capture of this kernel on one bench layer (same bytes
-                         # for gate, up and down)
-                         "traffic": QGEMV_TRAFFIC_BYTES},
+                         # capture of this kernel (per launch)
+                         "traffic": QGEMV_TRAFFIC_BYTES if not (world == 1 and STEP_CHAIN) else None},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk.summary(),
             "cpu_baseline": cpu,

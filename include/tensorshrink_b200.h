@@ -118,6 +118,64 @@ TS_API int ts_qlinear_gated(const ts_qweight* w, const void* gate_up, int x_dtyp
                size_t workspace_bytes, void* stream);
 
 /*
+ * One layer of a fused decode call. The reference runs each of these as a
+ * QuantLinear.forward (modules.py:819-940) between plain torch ops of its
+ * model (RMSNorm in front, the residual add behind); here they are folded
+ * into the decode kernel:
+ *   flags & TS_OP_GATED:   x rows hold [gate | up] (2 * cols): the input is
+ *                          silu(gate) * up (as ts_qlinear_gated);
+ *   flags & TS_OP_RMSNORM: x rows are fp32 (x_dtype TS_F32): the input is
+ *                          F.rms_norm(x, norm_weight, norm_eps) rounded to
+ *                          act_dtype, each token's mean square reduced in the
+ *                          kernel;
+ *   residual != NULL:      fp32 [M, rows] added to the result (may alias out).
+ * act_dtype: the activation dtype the staged input is rounded to (fp16/bf16;
+ * x_dtype for plain 16-bit inputs).
+ */
+#define TS_OP_GATED 1
+#define TS_OP_RMSNORM 2
+typedef struct ts_qlinear_op {
+  const ts_qweight* w;
+  const void* x;
+  int64_t x_row_stride;
+  int32_t x_dtype;
+  int32_t flags;
+  const void* bias;
+  int32_t bias_dtype;
+  int32_t out_dtype;
+  void* out;
+  int64_t out_row_stride;
+  const float* norm_weight;
+  float norm_eps;
+  int32_t act_dtype;
+  const float* residual;
+  int64_t residual_row_stride;
+} ts_qlinear_op;
+
+/*
+ * One fused layer call (decode-sized M; TS_ERR_UNSUPPORTED for calls the
+ * decode kernel does not take: then run the unfused ops and ts_qlinear).
+ * A call with no flags and no residual is ts_qlinear. Workspace as ts_qlinear.
+ */
+TS_API int ts_qlinear_ex(const ts_qlinear_op* op, int64_t M, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
+ * A chain of n_ops layers where op i + 1 reads what op i wrote (an MLP:
+ * gate_up then the gated down projection; or consecutive blocks). Results
+ * equal n_ops ts_qlinear_ex calls in stream order. When every layer takes the
+ * decode kernel in one pass with the same code layout (bits, group size,
+ * codebook, double quant) and n_ops <= ts_qlinear_chain_max(), the chain is
+ * ONE persistent launch: layer i + 1 waits (bounded) on a grid-wide counter
+ * for layer i while the weight tiles of the following layers already stream
+ * into shared memory. Otherwise the layers run as separate launches. The
+ * workspace must cover ts_qlinear_workspace_size() of every layer.
+ */
+TS_API int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, void* workspace,
+                            size_t workspace_bytes, void* stream);
+TS_API int ts_qlinear_chain_max(void);
+
+/*
  * Allocation-free variant of ts_qlinear (no counterpart in the reference):
  * same arguments minus the workspace. The decode kernel's scratch lives in a
  * fixed per-device array of ts_qlinear_noalloc_max_scratch() bytes (512 KiB)
@@ -202,6 +260,23 @@ TS_API int ts_ipc_open(const void* handle, void** ptr);
 TS_API int ts_ipc_close(void* ptr);
 TS_API int ts_allreduce_oneshot(void* const* peer_bufs, int rank, int world, int64_t cap, const float* in,
                                 const float* residual, float* out, int64_t n, int* err_flag, void* stream);
+
+/*
+ * Decode-step attention of the Llama-shaped decoder used to measure decode
+ * tok/s (no counterpart in the reference, whose models keep their own
+ * attention): for each of `batch` sequences, rotary embedding of the new q
+ * and k (rope_cos / rope_sin: fp32 [max_seq, head_dim / 2]), append of k and
+ * v to the bf16 caches at position *pos (device int64), and grouped-query
+ * attention over cache positions [0, min(attn_len, *pos + 1)).
+ * qkv: bf16 [batch, (n_q + 2 n_kv) head_dim] (q heads, then k, then v);
+ * caches: bf16 [batch][n_kv][max_seq][head_dim] with the given element
+ * strides; out: bf16 [batch, n_q head_dim].
+ */
+TS_API int ts_decode_attention(const void* qkv, int64_t qkv_row_stride, int batch, int n_q, int n_kv,
+                               int head_dim, const int64_t* pos, const float* rope_cos, const float* rope_sin,
+                               void* k_cache, void* v_cache, int64_t cache_batch_stride,
+                               int64_t cache_head_stride, int attn_len, int max_seq, void* out,
+                               int64_t out_row_stride, void* stream);
 
 /* Dense reconstruction W[rows, cols] in `out_dtype`.
  * Replaces triton_kernels.py:1114-1186 `dequantize_weight` (which covers only

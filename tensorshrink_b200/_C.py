@@ -66,6 +66,19 @@ class TsQuantOutputs(C.Structure):
     ]
 
 
+class TsQlinearOp(C.Structure):
+    """struct ts_qlinear_op (one layer of ts_qlinear_ex / ts_qlinear_chain)."""
+    _fields_ = [
+        ("w", C.POINTER(TsQWeight)), ("x", _vp), ("x_row_stride", _i64), ("x_dtype", _i32), ("flags", _i32),
+        ("bias", _vp), ("bias_dtype", _i32), ("out_dtype", _i32), ("out", _vp), ("out_row_stride", _i64),
+        ("norm_weight", _vp), ("norm_eps", C.c_float), ("act_dtype", _i32),
+        ("residual", _vp), ("residual_row_stride", _i64),
+    ]
+
+
+OP_GATED = 1
+OP_RMSNORM = 2
+
 # (name, restype, argtypes)
 _SIGNATURES = [
     ("ts_qlinear_workspace_size", C.c_size_t, [C.POINTER(TsQWeight), _i64]),
@@ -73,6 +86,9 @@ _SIGNATURES = [
                              C.c_int, _i64, _vp, C.c_size_t, _vp]),
     ("ts_qlinear_gated", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int, _vp,
                                    C.c_int, _i64, _vp, C.c_size_t, _vp]),
+    ("ts_qlinear_ex", C.c_int, [C.POINTER(TsQlinearOp), _i64, _vp, C.c_size_t, _vp]),
+    ("ts_qlinear_chain", C.c_int, [C.POINTER(TsQlinearOp), C.c_int, _i64, _vp, C.c_size_t, _vp]),
+    ("ts_qlinear_chain_max", C.c_int, []),
     ("ts_qlinear_noalloc_max_scratch", C.c_size_t, []),
     ("ts_qlinear_noalloc", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int,
                                      _vp, C.c_int, _i64, _vp]),
@@ -89,6 +105,8 @@ _SIGNATURES = [
     ("ts_ipc_open", C.c_int, [_vp, C.POINTER(_vp)]),
     ("ts_ipc_close", C.c_int, [_vp]),
     ("ts_allreduce_oneshot", C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, _i64, _vp, _vp, _vp, _i64, _vp, _vp]),
+    ("ts_decode_attention", C.c_int, [_vp, _i64, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp,
+                                      _i64, _i64, C.c_int, C.c_int, _vp, _i64, _vp]),
     ("ts_dequantize_weight", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, C.c_int, _vp]),
     ("ts_quantize_workspace_size", C.c_size_t, [C.POINTER(TsQuantParams)]),
     ("ts_quantize_pack", C.c_int, [_vp, C.c_int, C.POINTER(TsQuantParams), C.POINTER(TsQuantOutputs),

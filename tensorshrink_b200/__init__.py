@@ -29,6 +29,8 @@ from .gpu_quantize import (
     quantize_module_gpu,
 )
 from .kernels import (
+    ChainStep,
+    qlinear_chain,
     fused_quantized_linear,
     apply_outlier_correction,
     dequantize_weight,
@@ -41,5 +43,5 @@ __all__ = [
     "quantize_device", "quantize_device_adaptive", "dequantize_device", "relative_error", "QuantLinear", "quantize_module", "DEFAULT_SKIP_PATTERNS",
     "T5_EXTRA_SKIP_PATTERNS", "suggest_max_dequant_rows", "quantize_tensor_gpu",
     "quantize_tensor_gpu_adaptive", "quantize_module_gpu", "fused_quantized_linear",
-    "apply_outlier_correction", "dequantize_weight",
+    "apply_outlier_correction", "dequantize_weight", "ChainStep", "qlinear_chain",
 ]

@@ -18,9 +18,10 @@ namespace ts {
   size_t gemv_workspace_size(const ts_qweight& w);                                                   \
   size_t gemv_error_flag_offset();                                                                   \
   int gemv_max_tokens(const ts_qweight& w);                                                          \
-  int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,        \
-               const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,      \
-               void* workspace, size_t ws_bytes, cudaStream_t stream, int gated);                    \
+  int run_gemv(const GemvOp& op, int64_t M, void* workspace, size_t ws_bytes, cudaStream_t stream);  \
+  bool gemv_chain_ok(const GemvOp* ops, int n, int64_t M);                                           \
+  int run_gemv_chain(const GemvOp* ops, int n, int64_t M, void* workspace, size_t ws_bytes,          \
+                     cudaStream_t stream);                                                           \
   }
 TS_DECLARE_GEMV(gemv_v1)
 TS_DECLARE_GEMV(gemv_v2)
@@ -35,15 +36,28 @@ static size_t gemv_workspace_size(const ts_qweight& w) {
 }
 // Two CTAs per SM when that build takes all M tokens in one pass and the
 // workspace covers it; one CTA per SM otherwise.
-static int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
-                    const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
-                    void* workspace, size_t ws_bytes, cudaStream_t stream, int gated = 0) {
+static int run_gemv(const GemvOp& op, int64_t M, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  const ts_qweight& w = *op.w;
   if (gemv_v2::gemv_supported(w) && M <= gemv_v2::gemv_max_tokens(w) &&
       ws_bytes >= gemv_v2::gemv_workspace_size(w))
-    return gemv_v2::run_gemv(w, x, x_dtype, M, x_stride, bias, bias_dtype, out, out_dtype, out_stride,
-                             workspace, ws_bytes, stream, gated);
-  return gemv_v1::run_gemv(w, x, x_dtype, M, x_stride, bias, bias_dtype, out, out_dtype, out_stride,
-                           workspace, ws_bytes, stream, gated);
+    return gemv_v2::run_gemv(op, M, workspace, ws_bytes, stream);
+  return gemv_v1::run_gemv(op, M, workspace, ws_bytes, stream);
+}
+static GemvOp plain_op(const ts_qweight& w, const void* x, int x_dtype, int64_t x_stride, const void* bias,
+                       int bias_dtype, void* out, int out_dtype, int64_t out_stride, int gated) {
+  GemvOp op{};
+  op.w = &w;
+  op.x = x;
+  op.x_dtype = x_dtype;
+  op.x_stride = x_stride;
+  op.bias = bias;
+  op.bias_dtype = bias_dtype;
+  op.out = out;
+  op.out_dtype = out_dtype;
+  op.out_stride = out_stride;
+  op.gated = gated;
+  op.act_dtype = x_dtype;
+  return op;
 }
 int run_generic_qlinear(const ts_qweight& w, const void* x, int x_dtype, int64_t M,
                         int64_t x_stride, const void* bias, int bias_dtype, void* out,
@@ -213,8 +227,8 @@ int ts_qlinear(const ts_qweight* w, const void* x, int x_dtype, int64_t M, int64
                      counters_off, workspace_bytes, s);
   if (gemv_fits) {
     TS_REQUIRE(workspace != nullptr, "workspace is NULL (size %zu needed)", gemv_workspace_size(*w));
-    return run_gemv(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
-                    out_row_stride, workspace, workspace_bytes, s);
+    return run_gemv(plain_op(*w, x, x_dtype, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride, 0), M,
+                    workspace, workspace_bytes, s);
   }
   return run_generic_qlinear(*w, x, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype,
                              out_row_stride, s);
@@ -234,8 +248,93 @@ int ts_qlinear_gated(const ts_qweight* w, const void* gate_up, int x_dtype, int6
   TS_REQUIRE(w->n_outliers == 0 || w->outlier_row_ptr != nullptr, "qlinear needs the CSR outlier_row_ptr table");
   TS_UNSUPPORTED(gemv_supported(*w) && M <= gemv_v1::gemv_max_tokens(*w),
                  "gated qlinear runs in the decode kernel only (M=%lld)", (long long)M);
-  return run_gemv(*w, gate_up, x_dtype, M, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride,
-                  workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), 1);
+  return run_gemv(plain_op(*w, gate_up, x_dtype, x_row_stride, bias, bias_dtype, out, out_dtype, out_row_stride, 1),
+                  M, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// Validates one fused op and converts it to the decode kernel's form;
+// TS_ERR_UNSUPPORTED when the decode kernel does not take it.
+static int fused_op(const ts_qlinear_op* o, int64_t M, GemvOp& op) {
+  TS_REQUIRE(o != nullptr, "op is NULL");
+  int rc = check_qweight(o->w);
+  if (rc != TS_OK) return rc;
+  const ts_qweight& w = *o->w;
+  const bool gated = (o->flags & TS_OP_GATED) != 0, norm = (o->flags & TS_OP_RMSNORM) != 0;
+  TS_REQUIRE((o->flags & ~(TS_OP_GATED | TS_OP_RMSNORM)) == 0, "unknown op flags 0x%x", o->flags);
+  TS_UNSUPPORTED(!(gated && norm), "an op is gated or normalized, not both");
+  TS_UNSUPPORTED(valid_dtype(o->out_dtype), "out dtype must be fp16, bf16 or fp32");
+  TS_UNSUPPORTED(valid_act_dtype(o->act_dtype), "act dtype must be fp16 or bf16");
+  if (norm) {
+    TS_UNSUPPORTED(o->x_dtype == TS_F32, "RMSNorm ops take fp32 rows");
+    TS_REQUIRE(o->norm_weight != nullptr, "norm_weight is NULL");
+  } else {
+    TS_UNSUPPORTED(valid_act_dtype(o->x_dtype), "x dtype must be fp16 or bf16");
+    TS_UNSUPPORTED(o->x_dtype == o->act_dtype, "act dtype must equal x dtype for 16-bit inputs");
+  }
+  TS_REQUIRE(o->bias == nullptr || valid_dtype(o->bias_dtype), "bad bias dtype");
+  TS_REQUIRE(o->x != nullptr && o->out != nullptr, "x/out is NULL");
+  TS_REQUIRE(o->x_row_stride >= (gated ? 2 : 1) * w.cols && o->out_row_stride >= w.rows, "row strides too small");
+  TS_REQUIRE(o->residual == nullptr || o->residual_row_stride >= w.rows, "residual stride too small");
+  TS_REQUIRE(o->residual == nullptr || o->out_dtype == TS_F32 || o->residual != o->out,
+             "a residual aliasing out needs an fp32 out");
+  TS_REQUIRE(w.n_outliers == 0 || w.outlier_row_ptr != nullptr, "qlinear needs the CSR outlier_row_ptr table");
+  TS_UNSUPPORTED(gemv_supported(w) && M <= gemv_v1::gemv_max_tokens(w),
+                 "fused qlinear ops run in the decode kernel only (M=%lld)", (long long)M);
+  op = plain_op(w, o->x, o->x_dtype, o->x_row_stride, o->bias, o->bias_dtype, o->out, o->out_dtype,
+                o->out_row_stride, gated ? 1 : 0);
+  op.act_dtype = o->act_dtype;
+  op.norm_w = norm ? o->norm_weight : nullptr;
+  op.norm_eps = o->norm_eps;
+  op.residual = o->residual;
+  op.residual_stride = o->residual_row_stride;
+  return TS_OK;
+}
+
+int ts_qlinear_ex(const ts_qlinear_op* o, int64_t M, void* workspace, size_t workspace_bytes, void* stream) {
+  TS_REQUIRE(o != nullptr, "op is NULL");
+  TS_REQUIRE(M >= 0, "M < 0");
+  if (o->flags == 0 && o->residual == nullptr && o->x_dtype != TS_F32)
+    return ts_qlinear(o->w, o->x, o->x_dtype, M, o->x_row_stride, o->bias, o->bias_dtype, o->out, o->out_dtype,
+                      o->out_row_stride, workspace, workspace_bytes, stream);
+  if (M == 0 || (o->w && o->w->rows == 0)) return TS_OK;
+  GemvOp op;
+  const int rc = fused_op(o, M, op);
+  if (rc != TS_OK) return rc;
+  TS_REQUIRE(workspace != nullptr, "workspace is NULL");
+  return run_gemv(op, M, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_qlinear_chain_max(void) { return 8; }
+
+int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  TS_REQUIRE(ops != nullptr && n_ops >= 0, "bad op list");
+  TS_REQUIRE(M >= 0, "M < 0");
+  if (n_ops == 0 || M == 0) return TS_OK;
+  TS_REQUIRE(workspace != nullptr, "workspace is NULL");
+  // every op is validated before any runs: a chain runs whole or not at all
+  std::vector<GemvOp> g(n_ops);
+  for (int i = 0; i < n_ops; ++i) {
+    const int rc = fused_op(&ops[i], M, g[i]);
+    if (rc != TS_OK) return rc;
+    TS_REQUIRE(ops[i].w->rows > 0, "empty layer in a chain");
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n_ops > 1 && n_ops <= ts_qlinear_chain_max() && gemv_v1::gemv_chain_ok(g.data(), n_ops, M)) {
+    // the two-CTA-per-SM build when every layer fits it, else the one-CTA one
+    bool v2 = true;
+    for (int i = 0; i < n_ops && v2; ++i)
+      v2 = gemv_v2::gemv_supported(*g[i].w) && M <= gemv_v2::gemv_max_tokens(*g[i].w) &&
+           workspace_bytes >= gemv_v2::gemv_workspace_size(*g[i].w);
+    if (v2 && gemv_v2::gemv_chain_ok(g.data(), n_ops, M))
+      return gemv_v2::run_gemv_chain(g.data(), n_ops, M, workspace, workspace_bytes, s);
+    return gemv_v1::run_gemv_chain(g.data(), n_ops, M, workspace, workspace_bytes, s);
+  }
+  for (int i = 0; i < n_ops; ++i) {
+    const int rc = run_gemv(g[i], M, workspace, workspace_bytes, s);
+    if (rc != TS_OK) return rc;
+  }
+  return TS_OK;
 }
 
 int ts_apply_outlier_correction(float* out, int64_t M, int64_t N, int64_t out_row_stride,

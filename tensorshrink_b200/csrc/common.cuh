@@ -75,6 +75,13 @@ __device__ __forceinline__ float load_f(const void* p, int dtype, int64_t i) {
   return reinterpret_cast<const float*>(p)[i];
 }
 
+// the same through L2 only (data another CTA of the running kernel wrote)
+__device__ __forceinline__ float load_f_cg(const void* p, int dtype, int64_t i) {
+  if (dtype == TS_F16) return __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(p) + i)));
+  if (dtype == TS_BF16) return __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short*>(p) + i) << 16);
+  return __ldcg(reinterpret_cast<const float*>(p) + i);
+}
+
 __device__ __forceinline__ void store_f(void* p, int dtype, int64_t i, float v) {
   if (dtype == TS_F16)
     reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
@@ -118,6 +125,27 @@ __device__ __forceinline__ void pdl_wait_primary() {
 }
 
 // Decoded view of ts_qweight used by device code.
+// One decode-kernel layer call: y = W x (+ bias) (+ residual), x optionally
+// staged as silu(gate) * up of a [gate | up] row (gated) or as the RMSNorm of
+// an fp32 row (norm_w), rounded to act_dtype.
+struct GemvOp {
+  const ts_qweight* w;
+  const void* x;
+  int x_dtype;
+  int64_t x_stride;
+  const void* bias;
+  int bias_dtype;
+  void* out;
+  int out_dtype;
+  int64_t out_stride;
+  int gated;
+  const float* norm_w;
+  float norm_eps;
+  int act_dtype;
+  const float* residual;
+  int64_t residual_stride;
+};
+
 struct QW {
   const uint8_t* packed;
   const __half* scale;

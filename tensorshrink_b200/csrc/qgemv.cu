@@ -198,7 +198,24 @@ struct Args {
   int x_vec16;         // activation rows are 16-byte aligned
   int meta_bulk;       // metadata rows are 16-byte multiples: one 2-D copy per array per tile
   int dq_shift;        // log2(dq_group_size) when it is a power of two, else -1
+  int act_dtype;       // dtype the staged activations are rounded to (after the gate / the norm)
+  const float* norm_w; // RMSNorm weight: x rows are the fp32 residual stream, normalized while staged
+  float norm_eps;
+  const float* residual;     // fp32 [M, rows] added to the output, or nullptr
+  int64_t residual_stride;
 };
+
+// A chain of layers run by one persistent launch: layer i + 1 starts reading
+// its activations once every CTA has finished layer i (a grid-wide counter
+// in the workspace), while the producer warps keep streaming weight tiles of
+// the following layers into the ring. NL bounds the chain length.
+template <int NL>
+struct Chain {
+  Args L[NL];
+  int n;
+  int* sync;   // workspace: [done counter per layer boundary][exit counter]
+};
+constexpr int kMaxChain = 8;
 
 // super-group index of a flat (row, group) index
 __device__ __forceinline__ uint32_t dq_div(uint32_t flat, const Args& a) {
@@ -209,11 +226,37 @@ __device__ __forceinline__ uint32_t cta_of(uint64_t t, uint64_t U, uint64_t G) {
   return (uint32_t)(((t + 1) * G + U - 1) / U - 1);
 }
 
+// shared memory ahead of the stage ring: the ring's mbarriers and the CTA flags
+constexpr int kHeadBytes = 256;
+
+// Waits (bounded) until every CTA of the launch has finished the previous
+// layer of a chain: consumer thread 0 polls the layer's counter, the other
+// consumer threads wait at the named barrier.
+__device__ __forceinline__ void chain_wait(const int* done, const Args& a, volatile int* s_abort) {
+  if (threadIdx.x == 0) {
+    const uint64_t t_start = globaltimer_ns();
+    while (ld_acquire_gpu(done) < (int)gridDim.x) {
+      if (*s_abort) break;
+      if (globaltimer_ns() - t_start > a.wait_ns) {
+        atomicExch(a.err, 4);
+        *s_abort = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  named_bar_sync(1, kConsumerThreads);
+}
+
+// One layer of the launch, run by every warp of the CTA in its role. The ring
+// position (rs, rph) and the count of issued stages carry over from layer to
+// layer, so the producer streams the next layer's tiles as soon as stages
+// free up.
 template <int BITS, bool CB, bool DQ, int SEG>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
-    qgemv_kernel(const __grid_constant__ Args a) {
+__device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* full, uint64_t* empty, int* s_flag,
+                                           float* s_rstd, int& rs, uint32_t& rph, uint32_t& issued, int layer,
+                                           const int* chain_done) {
   using G = Geo<BITS>;
-  extern __shared__ __align__(128) char smem[];
   constexpr int LUT_BYTES = !CB ? 0 : (BITS == 2 ? 256 * 32 * 8 : 256 * 32 * 4);
   constexpr int E = DQ ? 4 : 2;                      // metadata elements per 32-bit word
   const int S = a.stages;
@@ -233,10 +276,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   int* o_col = o_ptr + a.max_owned_rows + 4;                                            // [kOutCap]
   uint32_t* o_dw = reinterpret_cast<uint32_t*>(o_col + kOutCap);   // [kOutCap / 2 + 1] fp16 deltas as words
   float* o_bias = reinterpret_cast<float*>(o_dw + kOutCap);                             // [owned rows]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(o_bias + a.max_owned_rows + 4);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + kMaxStages;
-  int* s_flag = reinterpret_cast<int*>(bars + 2 * kMaxStages);
   // set by the first wait that runs out: every role stops waiting and
   // unwinds (the producer first lets its copies in flight land)
   volatile int* s_abort = s_flag + 1;
@@ -246,32 +285,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // CTA b owns units [UQ b / G, UQ (b+1) / G) of `quantum` tiles each
+  // (CTAs past this layer's grid, in a chain sized for a larger layer, own none)
   const uint64_t Q = a.quantum, UQ = a.tiles / a.quantum, GR = a.grid;
-  const uint32_t t0 = (uint32_t)(UQ * blockIdx.x / GR * Q), t1 = (uint32_t)(UQ * (blockIdx.x + 1) / GR * Q);
+  const bool in_grid = blockIdx.x < a.grid;
+  const uint32_t t0 = in_grid ? (uint32_t)(UQ * blockIdx.x / GR * Q) : 0u;
+  const uint32_t t1 = in_grid ? (uint32_t)(UQ * (blockIdx.x + 1) / GR * Q) : 0u;
   const uint32_t KG = a.kgroups;
   const uint32_t NGR = (uint32_t)a.q.n_groups;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(full + i, a.meta_bulk ? 1 : 1 + 32);   // expect_tx arrival (+ 32 async-copy arrivals)
-      mbar_init(empty + i, kConsumerWarps);
-    }
-    *s_abort = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-
   // ------------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
-    pdl_launch_dependents();
     if (a.stall) return;
     uint32_t rb = t0 / KG, kg = t0 - rb * KG;
-    int s = 0;
-    uint32_t ph = 0;          // phase of the ring pass that stage s belongs to
-    uint32_t issued = 0;
+    int s = rs;
+    uint32_t ph = rph;        // phase of the ring pass that stage s belongs to
     for (uint32_t i = 0; t0 + i < t1; ++i) {
       // warp-uniform decisions: every lane takes part in the __syncwarp below
-      if (i >= (uint32_t)S && !__all_sync(0xffffffffu, mbar_wait_hint(empty + s, ph ^ 1, a.err, 1, a.wait_ns))) {
+      if (issued >= (uint32_t)S && !__all_sync(0xffffffffu, mbar_wait_hint(empty + s, ph ^ 1, a.err, 1, a.wait_ns))) {
         *s_abort = 1;
         break;
       }
@@ -354,11 +384,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       if (++s == S) { s = 0; ph ^= 1; }
     }
-    // let the copies still in flight (the last S issues at most) land before
-    // this CTA's shared memory goes away: after a timeout the consumers stop
-    // waiting for them (in a normal run these phases have completed already)
-    for (uint32_t k = issued > (uint32_t)S ? issued - S : 0; k < issued; ++k)
-      mbar_wait_hint(full + (k % S), (k / S) & 1, nullptr, 0, a.wait_ns);
+    rs = s;
+    rph = ph;
     return;
   }
 
@@ -417,8 +444,44 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       reinterpret_cast<__half*>(o_dw)[j + dl_off] = __ldg(a.q.odelta + o_base + j);
   }
 
-  // x is produced by the previous kernel in the stream (programmatic launch)
-  pdl_wait_primary();
+  // x is produced by the previous kernel in the stream (programmatic launch),
+  // or, in a chain, by the previous layer of this launch
+  if (layer == 0)
+    pdl_wait_primary();
+  else
+    chain_wait(chain_done + layer - 1, a, s_abort);
+  if (a.norm_w) {
+    // RMSNorm of each token's fp32 row: 1 / sqrt(mean(h^2) + eps), reduced
+    // over the consumer threads (warp shuffles, then the flush scratch)
+    float ss[kMaxTok];
+#pragma unroll
+    for (int n = 0; n < kMaxTok; ++n) ss[n] = 0.f;
+    const int64_t C = a.q.cols;
+#pragma unroll
+    for (int n = 0; n < kMaxTok; ++n) {
+      if (n >= a.mt) break;
+      const float* h = reinterpret_cast<const float*>(a.x) + (a.m0 + n) * a.x_stride;
+      for (int64_t k = threadIdx.x; k < C; k += kConsumerThreads) {
+        const float v = __ldcg(h + k);
+        ss[n] = fmaf(v, v, ss[n]);
+      }
+    }
+    float* red0 = red;   // the flush scratch, free until the first flush
+#pragma unroll
+    for (int n = 0; n < kMaxTok; ++n) {
+      float v = ss[n];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red0[warp * kMaxTok + n] = v;
+    }
+    named_bar_sync(1, kConsumerThreads);
+    if (threadIdx.x < a.mt) {
+      float t = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) t += red0[w * kMaxTok + threadIdx.x];
+      s_rstd[threadIdx.x] = rsqrtf(t / (float)C + a.norm_eps);
+    }
+    named_bar_sync(1, kConsumerThreads);
+  }
   {
     // one thread per 16 consecutive activations of one token: load, reduce the
     // segment's max |x| and sum across its threads, write the B fragments
@@ -435,9 +498,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       float v[16];
       // 16 activations at element offset `off` of the token's row
       auto load16 = [&](int64_t off, float (&o)[16]) {
-        if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
+        // (L2-coherent loads: in a chain x was written by this launch)
+        if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols && a.x_dtype == TS_F32) {
+          const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + off);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 f = __ldcg(p + j);
+            o[4 * j] = f.x;
+            o[4 * j + 1] = f.y;
+            o[4 * j + 2] = f.z;
+            o[4 * j + 3] = f.w;
+          }
+        } else if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
           const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + off);
-          const uint4 r0 = __ldg(p), r1 = __ldg(p + 1);
+          const uint4 r0 = __ldcg(p), r1 = __ldcg(p + 1);
           const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -453,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            o[j] = (live && k0 + j < (uint32_t)a.q.cols) ? load_f(a.x, a.x_dtype, off + j) : 0.f;
+            o[j] = (live && k0 + j < (uint32_t)a.q.cols) ? load_f_cg(a.x, a.x_dtype, off + j) : 0.f;
         }
       };
       load16(xo, v);
@@ -465,9 +539,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         load16(xo + a.q.cols, u);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const float sl = round_act(v[j] / (1.f + __expf(-v[j])), a.x_dtype);
-          v[j] = round_act(sl * u[j], a.x_dtype);
+          const float sl = round_act(v[j] / (1.f + __expf(-v[j])), a.act_dtype);
+          v[j] = round_act(sl * u[j], a.act_dtype);
         }
+      } else if (a.norm_w) {
+        // x = (h * rstd) * w, rounded to the activation dtype, as
+        // F.rms_norm(h, w).to(dtype) rounds it
+        const float rs = live ? s_rstd[n] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          v[j] = (live && k0 + j < (uint32_t)a.q.cols) ? round_act(v[j] * rs * __ldg(a.norm_w + k0 + j), a.act_dtype)
+                                                         : 0.f;
       }
       float mx = 0.f, sum = 0.f;
 #pragma unroll
@@ -656,8 +738,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const float4* sxa = sx + l * n_seg;
   const float4* sxb = sx + (4 + l) * n_seg;
 
-  int cs = 0;
-  uint32_t cph = 0;
+  int& cs = rs;          // consumers: the ring position carries over between layers
+  uint32_t& cph = rph;
   for (uint32_t i = 0; t0 + i < t1; ++i) {
     const int s = cs;
     // warp-uniform: the MMAs below need every lane; after any role's timeout
@@ -909,7 +991,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       if (started_here && last_kg) {
         if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
-          store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row, tot);
+          store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
+                  a.residual ? tot + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : tot);
       } else {
         const int slot = rb == first_rb ? 0 : 1;
         if (t < kTileRows * kMaxTok)
@@ -938,7 +1021,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
               sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) + t);
           }
           if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
-            store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row, sum);
+            store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
+                    a.residual ? sum + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : sum);
           if (t == 0) a.counters[rb] = 0;
         }
       }
@@ -950,6 +1034,65 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       started_here = true;
     } else {
       ++kg;
+    }
+  }
+}
+
+template <int BITS, bool CB, bool DQ, int SEG, int NL>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const __grid_constant__ Chain<NL> c) {
+  extern __shared__ __align__(128) char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  int* s_flag = reinterpret_cast<int*>(empty + kMaxStages);   // [0] flush arrival, [1] abort
+  float* s_rstd = reinterpret_cast<float*>(s_flag + 4);        // [kMaxTok] RMSNorm factors
+  char* body = smem + kHeadBytes;
+  const Args& a0 = c.L[0];
+  const int S = a0.stages;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full + i, a0.meta_bulk ? 1 : 1 + 32);   // expect_tx arrival (+ 32 async-copy arrivals)
+      mbar_init(empty + i, kConsumerWarps);
+    }
+    s_flag[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int n = NL == 1 ? 1 : c.n;
+  const bool producer = (threadIdx.x >> 5) == kConsumerWarps;
+  if (producer) pdl_launch_dependents();
+  int rs = 0;
+  uint32_t rph = 0, issued = 0;
+  for (int L = 0; L < n; ++L) {
+    gemv_layer<BITS, CB, DQ, SEG>(c.L[L], body, full, empty, s_flag, s_rstd, rs, rph, issued, L,
+                                  NL == 1 ? nullptr : c.sync);
+    if (!producer && NL > 1 && L + 1 < n) {
+      // every output of this CTA for layer L is stored: count it in
+      named_bar_sync(1, kConsumerThreads);
+      if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(c.sync + L, 1);
+      }
+    }
+  }
+  if (producer) {
+    // let the copies still in flight (the last S issues at most) land before
+    // this CTA's shared memory goes away: after a timeout the consumers stop
+    // waiting for them (in a normal run these phases have completed already)
+    for (uint32_t k = issued > (uint32_t)S ? issued - S : 0; k < issued; ++k)
+      mbar_wait_hint(full + (k % S), (k / S) & 1, nullptr, 0, a0.wait_ns);
+    return;
+  }
+  if (NL > 1 && n > 1) {
+    // the last CTA out zeroes the chain counters for the next launch (no CTA
+    // polls them any more once every CTA has counted itself out)
+    named_bar_sync(1, kConsumerThreads);
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(c.sync + kMaxChain, 1) == (int)gridDim.x - 1) {
+        for (int L = 0; L + 1 < n; ++L) c.sync[L] = 0;
+        c.sync[kMaxChain] = 0;
+        __threadfence();
+      }
     }
   }
 }
@@ -1037,7 +1180,7 @@ size_t fixed_smem(const ts_qweight& w, const Plan& p, int mt) {
          (size_t)p.max_owned_rows * gemv::kMaxTok * 4 +
          (size_t)gemv::kConsumerWarps * gemv::kTileRows * gemv::kMaxTok * 4 +
          (size_t)(p.max_owned_rows + 4) * 4 + (size_t)gemv::kOutCap * 8 + (size_t)(p.max_owned_rows + 4) * 4 +
-         2 * gemv::kMaxStages * 8 + 64;
+         gemv::kHeadBytes + 64;
 }
 
 size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024 / gemv::kCtasPerSm - (gemv::kCtasPerSm - 1) * 1024); }
@@ -1048,9 +1191,9 @@ int stages_for(const ts_qweight& w, const Plan& p, int mt) {
   return (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - f) / p.stage_bytes);
 }
 
-template <int BITS, bool CB, bool DQ, int SEG>
-int launch_one(const gemv::Args& a, cudaStream_t stream, size_t smem) {
-  auto kern = gemv::qgemv_kernel<BITS, CB, DQ, SEG>;
+template <int BITS, bool CB, bool DQ, int SEG, int NL>
+int launch_one(const gemv::Chain<NL>& c, uint32_t grid, cudaStream_t stream, size_t smem) {
+  auto kern = gemv::qgemv_kernel<BITS, CB, DQ, SEG, NL>;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -1061,7 +1204,7 @@ int launch_one(const gemv::Args& a, cudaStream_t stream, size_t smem) {
     configured_smem = smem;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.grid);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(gemv::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -1069,23 +1212,43 @@ int launch_one(const gemv::Args& a, cudaStream_t stream, size_t smem) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  TS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
+  cfg.numAttrs = NL == 1 ? 1 : 0;
+  if (NL > 1) {
+    // the layers of a chain wait for one another across CTAs, so every CTA
+    // must fit on the device at once (the waits are bounded all the same)
+    int per_sm = 0;
+    TS_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, gemv::kThreads, smem));
+    TS_UNSUPPORTED((int64_t)per_sm * sm_count() >= (int64_t)grid, "qlinear chain: %u CTAs do not fit at once",
+                   grid);
+  }
+  TS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, c));
   count_launch();
   return TS_OK;
 }
 
-template <int BITS, bool CB, bool DQ>
-int launch_seg(int seg, const gemv::Args& a, cudaStream_t s, size_t smem) {
-  if (seg == 1) return launch_one<BITS, CB, DQ, 1>(a, s, smem);
-  if (seg == 2) return launch_one<BITS, CB, DQ, 2>(a, s, smem);
-  return launch_one<BITS, CB, DQ, 4>(a, s, smem);
+template <int BITS, bool CB, bool DQ, int NL>
+int launch_seg(int seg, const gemv::Chain<NL>& c, uint32_t grid, cudaStream_t s, size_t smem) {
+  if (seg == 1) return launch_one<BITS, CB, DQ, 1, NL>(c, grid, s, smem);
+  if (seg == 2) return launch_one<BITS, CB, DQ, 2, NL>(c, grid, s, smem);
+  return launch_one<BITS, CB, DQ, 4, NL>(c, grid, s, smem);
 }
 
-template <int BITS>
-int launch_bits(bool cb, bool dq, int seg, const gemv::Args& a, cudaStream_t s, size_t smem) {
-  if (cb) return dq ? launch_seg<BITS, true, true>(seg, a, s, smem) : launch_seg<BITS, true, false>(seg, a, s, smem);
-  return dq ? launch_seg<BITS, false, true>(seg, a, s, smem) : launch_seg<BITS, false, false>(seg, a, s, smem);
+template <int BITS, int NL>
+int launch_bits(bool cb, bool dq, int seg, const gemv::Chain<NL>& c, uint32_t grid, cudaStream_t s, size_t smem) {
+  if (cb)
+    return dq ? launch_seg<BITS, true, true, NL>(seg, c, grid, s, smem)
+              : launch_seg<BITS, true, false, NL>(seg, c, grid, s, smem);
+  return dq ? launch_seg<BITS, false, true, NL>(seg, c, grid, s, smem)
+            : launch_seg<BITS, false, false, NL>(seg, c, grid, s, smem);
+}
+
+template <int NL>
+int launch_chain(const ts_qweight& w, int seg, const gemv::Chain<NL>& c, uint32_t grid, cudaStream_t s,
+                 size_t smem) {
+  const bool cb = w.codebook != nullptr, dq = w.dq_scale_codes != nullptr;
+  if (w.bits == 4) return launch_bits<4, NL>(cb, dq, seg, c, grid, s, smem);
+  if (w.bits == 2) return launch_bits<2, NL>(cb, dq, seg, c, grid, s, smem);
+  return launch_bits<8, NL>(cb, dq, seg, c, grid, s, smem);
 }
 
 }  // namespace
@@ -1139,31 +1302,31 @@ int gemv_max_tokens(const ts_qweight& w) {
   return 0;
 }
 
-int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t x_stride,
-             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t out_stride,
-             void* workspace, size_t ws_bytes, cudaStream_t stream, int gated) {
-  const int max_mt = gemv_max_tokens(w);
-  TS_UNSUPPORTED(max_mt > 0, "qlinear: activations of %lld columns do not fit in shared memory",
-                 (long long)w.cols);
-  TS_REQUIRE(ws_bytes >= gemv_workspace_size(w), "qlinear: workspace too small (%zu < %zu)", ws_bytes,
-             gemv_workspace_size(w));
-  const Plan p = make_plan(w);
-  gemv::Args a;
+namespace {
+
+// Kernel arguments of one layer (everything but the pass: m0, mt, stages).
+int make_args(const GemvOp& op, const Plan& p, void* workspace, gemv::Args& a) {
+  const ts_qweight& w = *op.w;
+  a = gemv::Args{};
   a.q = make_qw(w);
-  a.x = x;
-  a.x_dtype = x_dtype;
-  a.x_stride = x_stride;
-  a.bias = bias;
-  a.bias_dtype = bias_dtype;
-  a.out = out;
-  a.out_dtype = out_dtype;
-  a.out_stride = out_stride;
+  a.x = op.x;
+  a.x_dtype = op.x_dtype;
+  a.x_stride = op.x_stride;
+  a.bias = op.bias;
+  a.bias_dtype = op.bias_dtype;
+  a.out = op.out;
+  a.out_dtype = op.out_dtype;
+  a.out_stride = op.out_stride;
   char* ws = reinterpret_cast<char*>(workspace);
   a.partials = reinterpret_cast<float*>(ws);
   a.err = reinterpret_cast<int*>(ws + gemv_partials_bytes());
   a.wait_ns = wait_limit_ns();
-  a.stall = take_test_stall() ? 1 : 0;
-  a.gated = gated;
+  a.gated = op.gated;
+  a.act_dtype = op.act_dtype;
+  a.norm_w = op.norm_w;
+  a.norm_eps = op.norm_eps;
+  a.residual = op.residual;
+  a.residual_stride = op.residual_stride;
   a.counters = reinterpret_cast<int*>(ws + gemv_partials_bytes() + 256);
   a.tiles = p.tiles;
   a.kgroups = p.kgroups;
@@ -1179,7 +1342,8 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
   a.dq_shift = -1;
   if (w.dq_group_size > 0 && (w.dq_group_size & (w.dq_group_size - 1)) == 0) a.dq_shift = ilog2(w.dq_group_size);
   const bool dq = w.dq_scale_codes != nullptr;
-  a.x_vec16 = is_aligned(x, 16) && (x_stride * 2) % 16 == 0 && (!gated || (w.cols * 2) % 16 == 0);
+  const int64_t esz = op.x_dtype == TS_F32 ? 4 : 2;
+  a.x_vec16 = is_aligned(op.x, 16) && (op.x_stride * esz) % 16 == 0 && (!op.gated || (w.cols * esz) % 16 == 0);
   a.meta_bulk = p.meta_bulk ? 1 : 0;
   if (p.meta_bulk) {
     const CUtensorMapDataType t = dq ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
@@ -1193,22 +1357,86 @@ int run_gemv(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_t
                         CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != TS_OK) return rc;
   }
-  const bool cb = w.codebook != nullptr;
-  int rc = TS_OK;
+  return TS_OK;
+}
+
+}  // namespace
+
+int run_gemv(const GemvOp& op, int64_t M, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  const ts_qweight& w = *op.w;
+  const int max_mt = gemv_max_tokens(w);
+  TS_UNSUPPORTED(max_mt > 0, "qlinear: activations of %lld columns do not fit in shared memory",
+                 (long long)w.cols);
+  TS_REQUIRE(ws_bytes >= gemv_workspace_size(w), "qlinear: workspace too small (%zu < %zu)", ws_bytes,
+             gemv_workspace_size(w));
+  const Plan p = make_plan(w);
+  gemv::Chain<1> c;
+  c.n = 1;
+  c.sync = nullptr;
+  gemv::Args& a = c.L[0];
+  int rc = make_args(op, p, workspace, a);
+  if (rc != TS_OK) return rc;
+  a.stall = take_test_stall() ? 1 : 0;
   for (int64_t m0 = 0; m0 < M; m0 += max_mt) {
     a.m0 = m0;
     a.mt = (int)std::min<int64_t>(max_mt, M - m0);
     a.stages = stages_for(w, p, a.mt);
     const size_t smem = fixed_smem(w, p, a.mt) + (size_t)a.stages * p.stage_bytes;
-    if (w.bits == 4)
-      rc = launch_bits<4>(cb, dq, p.seg_chunks, a, stream, smem);
-    else if (w.bits == 2)
-      rc = launch_bits<2>(cb, dq, p.seg_chunks, a, stream, smem);
-    else
-      rc = launch_bits<8>(cb, dq, p.seg_chunks, a, stream, smem);
+    rc = launch_chain<1>(w, p.seg_chunks, c, p.grid, stream, smem);
     if (rc != TS_OK) return rc;
   }
   return TS_OK;
+}
+
+// Whether run_gemv_chain takes these layers: one pass each (M tokens), the
+// same kernel instantiation and stage layout for all, at most kMaxChain.
+bool gemv_chain_ok(const GemvOp* ops, int n, int64_t M) {
+  if (n < 1 || n > gemv::kMaxChain || M < 1) return false;
+  const ts_qweight& w0 = *ops[0].w;
+  const Plan p0 = make_plan(w0);
+  for (int i = 0; i < n; ++i) {
+    const ts_qweight& w = *ops[i].w;
+    if (!gemv_supported(w) || M > gemv_max_tokens(w)) return false;
+    if (w.bits != w0.bits || w.group_size != w0.group_size || (w.codebook != nullptr) != (w0.codebook != nullptr) ||
+        (w.dq_scale_codes != nullptr) != (w0.dq_scale_codes != nullptr))
+      return false;
+    const Plan p = make_plan(w);
+    if (p.seg_chunks != p0.seg_chunks || p.stage_bytes != p0.stage_bytes || p.meta_bulk != p0.meta_bulk) return false;
+  }
+  return true;
+}
+
+int run_gemv_chain(const GemvOp* ops, int n, int64_t M, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  TS_UNSUPPORTED(gemv_chain_ok(ops, n, M), "these layers do not form one decode chain");
+  gemv::Chain<gemv::kMaxChain> c;
+  c.n = n;
+  c.sync = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + gemv_partials_bytes() + 64);
+  size_t fixed = 0;
+  uint32_t grid = 1;
+  int stages = gemv::kMaxStages;
+  int seg = 0, stage_bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    const ts_qweight& w = *ops[i].w;
+    TS_REQUIRE(ws_bytes >= gemv_workspace_size(w), "qlinear chain: workspace too small (%zu < %zu)", ws_bytes,
+               gemv_workspace_size(w));
+    const Plan p = make_plan(w);
+    int rc = make_args(ops[i], p, workspace, c.L[i]);
+    if (rc != TS_OK) return rc;
+    c.L[i].m0 = 0;
+    c.L[i].mt = (int)M;
+    c.L[i].stall = 0;
+    fixed = std::max(fixed, fixed_smem(w, p, (int)M));
+    grid = std::max(grid, p.grid);
+    seg = p.seg_chunks;
+    stage_bytes = p.stage_bytes;
+  }
+  TS_UNSUPPORTED(fixed < smem_cap(), "qlinear chain: shared memory");
+  stages = (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - fixed) / stage_bytes);
+  TS_UNSUPPORTED(stages >= 2, "qlinear chain: shared memory for two stages");
+  c.L[0].stall = take_test_stall() ? 1 : 0;
+  for (int i = 0; i < n; ++i) c.L[i].stages = stages;
+  const size_t smem = fixed + (size_t)stages * stage_bytes;
+  return launch_chain<gemv::kMaxChain>(*ops[0].w, seg, c, grid, stream, smem);
 }
 
 }  // namespace TS_GEMV_NS

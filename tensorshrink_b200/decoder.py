@@ -236,6 +236,11 @@ class QuantDecoder(nn.Module):
         shape = (cfg.n_layers, max_batch, nkv, max_seq, D)
         self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
         self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        # decode steps through the fused kernels (RMSNorm staged in the
+        # projections, residual adds in their epilogues, one attention kernel,
+        # the MLP as one chained launch); False: the plain torch + qlinear ops
+        self.fused_decode = True
+        self._dbufs = {}
 
     def _vocab_bounds(self, rank):
         per = -(-self.cfg.vocab // self.world)
@@ -293,6 +298,49 @@ class QuantDecoder(nn.Module):
         gu = layer.gate_up(x)
         return self._reduce_add(layer.down_proj.gated(gu, torch.float32), h)
 
+    def _decode_buffers(self, B: int) -> dict:
+        bufs = self._dbufs.get(B)
+        if bufs is None:
+            l0 = self.layers[0]
+            D, dev = self.cfg.head_dim, self.device
+            bufs = {"qkv": torch.empty(B, sum(l0.splits_qkv), dtype=torch.bfloat16, device=dev),
+                    "attn": torch.empty(B, l0.n_heads_local * D, dtype=torch.bfloat16, device=dev),
+                    "gu": torch.empty(B, 2 * l0.split_gate, dtype=torch.bfloat16, device=dev),
+                    "part": torch.empty(B, self.cfg.hidden, dtype=torch.float32, device=dev)}
+            self._dbufs[B] = bufs
+        return bufs
+
+    def _layer_decode(self, i: int, layer: QuantDecoderLayer, h: torch.Tensor, pos: torch.Tensor,
+                      attn_len: int) -> torch.Tensor:
+        """One layer of a decode step on the fp32 residual stream h [B, H],
+        updated in place: q/k/v projection with the input RMSNorm staged in
+        its kernel, the attention kernel (rope + cache append + GQA), then
+        o_proj (+ residual), gate/up (post RMSNorm staged) and the gated down
+        projection (+ residual) as one chained launch. With tensor
+        parallelism the row-parallel partials go through the exchange (or
+        NCCL) with the residual add fused there."""
+        from .kernels import ChainStep, decode_attention, qlinear_chain
+        cfg = self.cfg
+        b = self._decode_buffers(h.shape[0])
+        bf16 = torch.bfloat16
+        qkv, gu = layer.qkv.local, layer.gate_up.local
+        qlinear_chain([ChainStep(qkv.qweight(), h, b["qkv"], bias=qkv.bias, norm_weight=layer.input_norm,
+                                 norm_eps=cfg.rms_eps, act_dtype=bf16)])
+        decode_attention(b["qkv"], layer.n_heads_local, layer.n_kv_local, cfg.head_dim, pos, self.rope_cos,
+                         self.rope_sin, self.k_cache[i], self.v_cache[i], attn_len, out=b["attn"])
+        o, down = layer.o_proj.local, layer.down_proj.local
+        up_steps = [ChainStep(gu.qweight(), h, b["gu"], bias=gu.bias, norm_weight=layer.post_norm,
+                              norm_eps=cfg.rms_eps, act_dtype=bf16)]
+        if self.world == 1:
+            qlinear_chain([ChainStep(o.qweight(), b["attn"], h, bias=o.bias, residual=h)] + up_steps
+                          + [ChainStep(down.qweight(), b["gu"], h, bias=down.bias, gated=True, residual=h)])
+            return h
+        qlinear_chain([ChainStep(o.qweight(), b["attn"], b["part"], bias=o.bias if self.rank == 0 else None)])
+        h = self._reduce_add(b["part"], h)
+        qlinear_chain(up_steps + [ChainStep(down.qweight(), b["gu"], b["part"],
+                                            bias=down.bias if self.rank == 0 else None, gated=True)])
+        return self._reduce_add(b["part"], h)
+
     def _next_token(self, h_last: torch.Tensor) -> torch.Tensor:
         """Greedy next token: global argmax over the vocabulary shards."""
         x = _rms_norm(h_last, self.final_norm, self.cfg.rms_eps)
@@ -342,8 +390,13 @@ class QuantDecoder(nn.Module):
         int64 device tensor, advanced by the caller). Attention reads the first
         `attn_len` cache positions (default all), masked to those <= pos.
         Returns the next tokens (or the fp32 logits)."""
-        h = self.embed[tokens][:, None, :].float()
         L = attn_len or self.max_seq
+        if self.fused_decode:
+            h = self.embed[tokens].float()
+            for i, layer in enumerate(self.layers):
+                h = self._layer_decode(i, layer, h, pos, L)
+            return self._logits(h) if return_logits else self._next_token(h)
+        h = self.embed[tokens][:, None, :].float()
         mask = (torch.arange(L, device=h.device) <= pos)[None, None, None, :]
         for i, layer in enumerate(self.layers):
             h = self._layer(i, layer, h, pos, mask, L)

@@ -19,6 +19,7 @@ keep the reference signatures (tensorshrink triton_kernels.py:714-739,
 
 from __future__ import annotations
 
+import ctypes as C
 import threading
 from typing import Dict, List, Optional, Tuple
 
@@ -241,6 +242,117 @@ def qlinear_gated(gate_up: torch.Tensor, qw: _C.TsQWeight, bias: Optional[torch.
         g, u = gate_up[:, :K], gate_up[:, K:2 * K]
         return qlinear((torch.nn.functional.silu(g) * u).contiguous(), qw, bias, out_dtype, out=out)
     _C.check(rc, "ts_qlinear_gated")
+    return out
+
+
+class ChainStep:
+    """One layer of `qlinear_chain`: out = W x' (+ bias) (+ residual), with x'
+    = x, or silu(gate) * up of x = [gate | up] (`gated`), or
+    F.rms_norm(x, norm_weight, norm_eps) of fp32 rows (`norm_weight`),
+    rounded to `act_dtype`. `residual` (fp32 [M, rows]) may be `out`."""
+
+    __slots__ = ("qw", "x", "out", "bias", "gated", "norm_weight", "norm_eps", "act_dtype", "residual")
+
+    def __init__(self, qw: _C.TsQWeight, x: torch.Tensor, out: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 gated: bool = False, norm_weight: Optional[torch.Tensor] = None, norm_eps: float = 1e-5,
+                 act_dtype: Optional[torch.dtype] = None, residual: Optional[torch.Tensor] = None):
+        self.qw, self.x, self.out, self.bias = qw, x, out, bias
+        self.gated, self.norm_weight, self.norm_eps = gated, norm_weight, norm_eps
+        self.act_dtype = act_dtype if act_dtype is not None else (torch.bfloat16 if x.dtype == torch.float32
+                                                                  else x.dtype)
+        self.residual = residual
+
+    def to_c(self) -> _C.TsQlinearOp:
+        for t, name in ((self.x, "x"), (self.out, "out"), (self.residual, "residual")):
+            if t is not None and (t.dim() != 2 or t.stride(-1) != 1):
+                raise ValueError(f"chain step {name} must be a 2-D row-major tensor")
+        if self.norm_weight is not None and (self.norm_weight.dtype != torch.float32
+                                             or not self.norm_weight.is_contiguous()):
+            raise ValueError("norm_weight must be a contiguous fp32 tensor")
+        if self.residual is not None and self.residual.dtype != torch.float32:
+            raise ValueError("residual must be fp32")
+        op = _C.TsQlinearOp()
+        op.w = C.pointer(self.qw)
+        op.x = self.x.data_ptr()
+        op.x_row_stride = int(self.x.stride(0))
+        op.x_dtype = dtype_code(self.x.dtype)
+        op.flags = (_C.OP_GATED if self.gated else 0) | (_C.OP_RMSNORM if self.norm_weight is not None else 0)
+        op.bias = _ptr(self.bias)
+        op.bias_dtype = dtype_code(self.bias.dtype) if self.bias is not None else 0
+        op.out = self.out.data_ptr()
+        op.out_dtype = dtype_code(self.out.dtype)
+        op.out_row_stride = int(self.out.stride(0))
+        op.norm_weight = _ptr(self.norm_weight)
+        op.norm_eps = float(self.norm_eps)
+        op.act_dtype = dtype_code(self.act_dtype)
+        op.residual = _ptr(self.residual)
+        op.residual_row_stride = int(self.residual.stride(0)) if self.residual is not None else 0
+        return op
+
+    def run_unfused(self) -> None:
+        """The same layer from separate torch ops and `qlinear` (calls the
+        decode kernel does not take)."""
+        x = self.x
+        if self.gated:
+            K = int(self.qw.cols)
+            x = (torch.nn.functional.silu(x[:, :K]) * x[:, K:2 * K]).to(self.act_dtype)
+        elif self.norm_weight is not None:
+            x = torch.nn.functional.rms_norm(x, (x.shape[-1],), self.norm_weight, self.norm_eps).to(self.act_dtype)
+        if self.residual is None:
+            qlinear(x.contiguous(), self.qw, self.bias, self.out.dtype, out=self.out)
+        else:
+            y = qlinear(x.contiguous(), self.qw, self.bias, torch.float32)
+            self.out.copy_(self.residual + y)
+
+
+def qlinear_chain(steps: List[ChainStep]) -> None:
+    """Run `steps` in order (step i + 1 may read what step i wrote) through
+    `ts_qlinear_chain`: for decode-sized M one persistent launch when the
+    layers share a code layout, else one decode launch each; calls the decode
+    kernel does not take run unfused, step by step."""
+    if not steps:
+        return
+    lib = _C.load()
+    M = int(steps[0].x.shape[0])
+    dev = steps[0].x.device
+    if any(int(st.x.shape[0]) != M or int(st.out.shape[0]) != M for st in steps):
+        raise ValueError("every chain step must have the same number of rows")
+    need = max(int(lib.ts_qlinear_workspace_size(st.qw, M)) for st in steps)
+    ws = workspace_for(dev, need)
+    arr = (_C.TsQlinearOp * len(steps))(*[st.to_c() for st in steps])
+    rc = lib.ts_qlinear_chain(arr, len(steps), M, ws.data_ptr(), int(ws.numel()), _stream_handle(dev))
+    if rc == -2:      # validated before anything ran: run the layers unfused
+        for st in steps:
+            st.run_unfused()
+        return
+    _C.check(rc, "ts_qlinear_chain")
+
+
+def decode_attention(qkv: torch.Tensor, n_q: int, n_kv: int, head_dim: int, pos: torch.Tensor,
+                     rope_cos: torch.Tensor, rope_sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     attn_len: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One decode step of grouped-query attention (`ts_decode_attention`):
+    ropes the new q/k of `qkv` ([B, (n_q + 2 n_kv) D] bf16) at position
+    `pos` (int64 device tensor, one element), writes k/v into this layer's
+    caches ([B', n_kv, max_seq, D] bf16, B' >= B) and attends over positions
+    < min(attn_len, pos + 1). Returns [B, n_q D] bf16."""
+    lib = _C.load()
+    B = int(qkv.shape[0])
+    if qkv.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError("decode_attention takes bf16 q/k/v and caches")
+    if k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1 or k_cache.stride(-2) != head_dim:
+        raise ValueError("the caches must share a [B, n_kv, max_seq, D] row-major layout")
+    if pos.dtype != torch.int64 or rope_cos.dtype != torch.float32 or not rope_cos.is_contiguous() \
+            or not rope_sin.is_contiguous():
+        raise ValueError("pos must be int64, the rotary tables contiguous fp32")
+    if out is None:
+        out = torch.empty(B, n_q * head_dim, dtype=torch.bfloat16, device=qkv.device)
+    rc = lib.ts_decode_attention(qkv.data_ptr(), int(qkv.stride(0)), B, n_q, n_kv, head_dim, pos.data_ptr(),
+                                 rope_cos.data_ptr(), rope_sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                 int(k_cache.stride(0)), int(k_cache.stride(1)), int(attn_len),
+                                 int(k_cache.shape[2]), out.data_ptr(), int(out.stride(0)),
+                                 _stream_handle(qkv.device))
+    _C.check(rc, "ts_decode_attention")
     return out
 
 

@@ -114,3 +114,53 @@ def test_cuda_graph_decode_matches_eager(model):
     torch.cuda.synchronize()
     for a, b in zip(eager, got):
         assert torch.equal(a, b)
+
+
+def test_fused_decode_matches_unfused(model):
+    """The fused decode step (norms staged in the projections, residual
+    epilogues, the attention kernel, chained MLP) against the plain torch +
+    qlinear step on the same cache contents."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    tokens = torch.randint(0, model.cfg.vocab, (2, 7), device="cuda", generator=g)
+    pos = torch.tensor([7], device="cuda")
+    nxt = torch.randint(0, model.cfg.vocab, (2,), device="cuda", generator=g)
+    model.prefill(tokens)
+    model.fused_decode = False
+    try:
+        ref = model.decode_step(nxt, pos, attn_len=16, return_logits=True)
+    finally:
+        model.fused_decode = True
+    model.prefill(tokens)
+    got = model.decode_step(nxt, pos, attn_len=16, return_logits=True)
+    assert ((got - ref).abs().max() / ref.abs().max()).item() < 1e-2
+
+
+@pytest.mark.parametrize("B,nq,nkv,pos,L", [(1, 8, 2, 0, 8), (2, 8, 2, 5, 16), (3, 4, 4, 20, 16), (1, 16, 2, 40, 64)])
+def test_decode_attention_kernel_matches_sdpa(B, nq, nkv, pos, L):
+    from tensorshrink_b200.kernels import decode_attention
+    D, S = 64, 64
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + pos)
+    qkv = torch.randn(B, (nq + 2 * nkv) * D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, nkv, S, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, nkv, S, D, device="cuda", generator=g).to(torch.bfloat16)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    ang = torch.outer(torch.arange(S, device="cuda", dtype=torch.float32), inv)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    kref, vref = kc.clone(), vc.clone()
+
+    def rope(x):   # x [B, h, D] at position pos
+        x1, x2 = x.float().chunk(2, dim=-1)
+        c, s = cos[pos], sin[pos]
+        return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1).to(torch.bfloat16)
+
+    q = rope(qkv[:, :nq * D].view(B, nq, D))
+    k = rope(qkv[:, nq * D:(nq + nkv) * D].view(B, nkv, D))
+    v = qkv[:, (nq + nkv) * D:].view(B, nkv, D)
+    kref[:, :, pos] = k
+    vref[:, :, pos] = v
+    mask = (torch.arange(L, device="cuda") <= pos)[None, None, None, :]
+    ref = F.scaled_dot_product_attention(q[:, :, None].float(), kref[:, :, :L].float(), vref[:, :, :L].float(),
+                                         attn_mask=mask, enable_gqa=True)[:, :, 0].reshape(B, nq * D)
+    out = decode_attention(qkv, nq, nkv, D, torch.tensor([pos], device="cuda"), cos, sin, kc, vc, L)
+    assert torch.equal(kc, kref) and torch.equal(vc, vref)
+    assert ((out.float() - ref).abs().max()).item() < 2e-2
