@@ -476,7 +476,10 @@ def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32
            "layer_bits": model.layer_bits, "packed_bytes_all_ranks": int(packed),
            "parallelism": (f"tp x{world}, " + ("NCCL" if exchange is None else "one-shot NVLink all-reduce kernel"))
                           if world > 1 else "single GPU",
-           "attention": "plain torch SDPA over a static bf16 KV cache (outside the measured path)",
+           "decode_path": ("per layer: q/k/v GEMV with the input RMSNorm staged in the kernel, the decode attention "
+                           "kernel (rope + cache append + GQA), then o_proj (+residual), gate|up (post RMSNorm "
+                           "staged) and the gated down projection (+residual) as one chained launch (B <= 8; larger "
+                           "batches run the same ops unfused)"),
            "decode": []}
     attn_len = ctx + steps + 8
     for B in batches:
@@ -485,11 +488,25 @@ def decoder_measure(device, world, timed, batches=(1, 16, 64), ctx=128, steps=32
         runner = CUDAGraphDecoder(model, B, attn_len=attn_len)
         model.prefill(tokens)
         runner.start(first, ctx)
+        torch.cuda.nvtx.range_push("decode")
         ms = timed(runner.step, steps) / steps
-        res["decode"].append({"batch": B, "context": ctx, "ms_per_step": round(ms, 4),
-                              "tokens_per_s": round(B / (ms * 1e-3), 1),
-                              "packed_GB/s": round(packed / (ms * 1e-3) / 1e9, 1)})
+        torch.cuda.nvtx.range_pop()
+        entry = {"batch": B, "context": ctx, "ms_per_step": round(ms, 4),
+                 "tokens_per_s": round(B / (ms * 1e-3), 1),
+                 "packed_GB/s": round(packed / (ms * 1e-3) / 1e9, 1)}
         del runner
+        if B == batches[0]:
+            # the same step from unfused torch ops + one qlinear launch per projection
+            model.fused_decode = False
+            model.prefill(tokens)
+            runner = CUDAGraphDecoder(model, B, attn_len=attn_len)
+            model.prefill(tokens)
+            runner.start(first, ctx)
+            ms_u = timed(runner.step, steps) / steps
+            entry["unfused_ms_per_step"] = round(ms_u, 4)
+            del runner
+            model.fused_decode = True
+        res["decode"].append(entry)
     if prefill:
         tokens = torch.randint(0, cfg.vocab, (1, 2048), device=device, generator=g)
         model.prefill(tokens)
@@ -583,9 +600,12 @@ def run_ours(args, rank, world, device):
     # per block: gate|up + gated down chained; whole step: one launch
     reps = max(args.steps, 10)
     variants = {}
-    for name, mode in (("per_layer", None), ("chain_per_block", "block"), ("chain_step", "step")):
+    for name, mode in (("per_layer", None), ("chain_per_block", "block"), ("chain_step", "step"),
+                       ("chain_step_1cta", "step")):
         if world > 1 and mode:
             continue
+        if name.endswith("_1cta"):
+            os.environ["TS_CHAIN_CTAS_PER_SM"] = "1"
         vx = torch.randn(M, HIDDEN, device=device).to(torch.bfloat16)
         for _ in range(2):
             mlp_step(blocks, vx, world, exchange, chain=mode)
@@ -600,6 +620,7 @@ def run_ours(args, rank, world, device):
         vms = timed(vg.replay, reps) / reps
         variants[name] = {"GB/s": round(bytes_job / (vms * 1e-3) / 1e9, 1), "ms_per_step": round(vms, 5),
                           "launches_per_step": int(nl)}
+        os.environ.pop("TS_CHAIN_CTAS_PER_SM", None)
         del vg
     n_layers = 2 * len(blocks)
     if world == 1 and STEP_CHAIN:
@@ -981,6 +1002,8 @@ def main():
                                                        "library's one-shot all-reduce kernel")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="--impl reference: skip the reference's own CUDA/Triton timing")
+    ap.add_argument("--only", choices=("decoder",), default=None,
+                    help="run one study alone (short; for launch lists): the 8B decoder at batch 1")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()
@@ -1001,6 +1024,20 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=device)
+    if args.only == "decoder":
+        def timed_only(fn, k):
+            torch.cuda.synchronize(device)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(k):
+                fn()
+            e.record()
+            torch.cuda.synchronize(device)
+            return s.elapsed_time(e)
+        out = decoder_measure(device, world, timed_only, batches=(1,), steps=args.steps, prefill=False)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return
     out = run_ours(args, rank, world, device)
     if rank == 0:
         print(json.dumps(out), flush=True)

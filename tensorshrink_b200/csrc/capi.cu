@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -321,8 +322,10 @@ int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, void* works
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (n_ops > 1 && n_ops <= ts_qlinear_chain_max() && gemv_v1::gemv_chain_ok(g.data(), n_ops, M)) {
-    // the two-CTA-per-SM build when every layer fits it, else the one-CTA one
-    bool v2 = true;
+    // the two-CTA-per-SM build when every layer fits it, else the one-CTA
+    // one; TS_CHAIN_CTAS_PER_SM=1 selects the one-CTA build (tuning knob)
+    const char* knob = getenv("TS_CHAIN_CTAS_PER_SM");
+    bool v2 = !(knob && knob[0] == '1');
     for (int i = 0; i < n_ops && v2; ++i)
       v2 = gemv_v2::gemv_supported(*g[i].w) && M <= gemv_v2::gemv_max_tokens(*g[i].w) &&
            workspace_bytes >= gemv_v2::gemv_workspace_size(*g[i].w);

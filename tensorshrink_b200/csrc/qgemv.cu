@@ -342,11 +342,6 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
                       (lane == 0 ? a.q.dqs_meta : a.q.dqg_meta) + sup_al, sup_bytes, full + s);
         }
       } else {
-        if (lane == 0) mbar_arrive_expect_tx(full + s, nrows * rbytes);
-        __syncwarp();
-        if (lane < (int)nrows)
-          bulk_load(st + lane * kPitch,
-                    a.q.packed + (size_t)(row0 + lane) * (size_t)a.q.row_bytes + (size_t)kg * kTileK, rbytes, full + s);
         // unaligned metadata: 4-byte async copies of the aligned-down words
         for (int ar = 0; ar < 2 * kTileRows; ++ar) {
           const int arr = ar / kTileRows, r = ar - arr * kTileRows;
@@ -375,7 +370,15 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
             cp_async4(sup + kMaxSupers + j, a.q.dqg_meta + (in ? sidx : 0u), in ? 4 : 0);
           }
         }
-        cp_async_arrive(full + s);
+        // every lane's copies are tracked by the barrier (each registers a
+        // pending arrival now) before lane 0's own arrival can end the phase
+        cp_async_arrive_inc(full + s);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(full + s, nrows * rbytes);
+        __syncwarp();
+        if (lane < (int)nrows)
+          bulk_load(st + lane * kPitch,
+                    a.q.packed + (size_t)(row0 + lane) * (size_t)a.q.row_bytes + (size_t)kg * kTileK, rbytes, full + s);
       }
       ++issued;
       if (++kg == KG) {
@@ -1050,7 +1053,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const __gri
   const int S = a0.stages;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(full + i, a0.meta_bulk ? 1 : 1 + 32);   // expect_tx arrival (+ 32 async-copy arrivals)
+      mbar_init(full + i, 1);   // the producer's expect_tx arrival (async-copy arrivals register themselves)
       mbar_init(empty + i, kConsumerWarps);
     }
     s_flag[1] = 0;
@@ -1401,7 +1404,7 @@ bool gemv_chain_ok(const GemvOp* ops, int n, int64_t M) {
         (w.dq_scale_codes != nullptr) != (w0.dq_scale_codes != nullptr))
       return false;
     const Plan p = make_plan(w);
-    if (p.seg_chunks != p0.seg_chunks || p.stage_bytes != p0.stage_bytes || p.meta_bulk != p0.meta_bulk) return false;
+    if (p.seg_chunks != p0.seg_chunks) return false;
   }
   return true;
 }
@@ -1428,13 +1431,16 @@ int run_gemv_chain(const GemvOp* ops, int n, int64_t M, void* workspace, size_t 
     fixed = std::max(fixed, fixed_smem(w, p, (int)M));
     grid = std::max(grid, p.grid);
     seg = p.seg_chunks;
-    stage_bytes = p.stage_bytes;
+    stage_bytes = std::max(stage_bytes, p.stage_bytes);   // rows first, then the layer's metadata
   }
   TS_UNSUPPORTED(fixed < smem_cap(), "qlinear chain: shared memory");
   stages = (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - fixed) / stage_bytes);
   TS_UNSUPPORTED(stages >= 2, "qlinear chain: shared memory for two stages");
   c.L[0].stall = take_test_stall() ? 1 : 0;
-  for (int i = 0; i < n; ++i) c.L[i].stages = stages;
+  for (int i = 0; i < n; ++i) {
+    c.L[i].stages = stages;
+    c.L[i].stage_bytes = stage_bytes;
+  }
   const size_t smem = fixed + (size_t)stages * stage_bytes;
   return launch_chain<gemv::kMaxChain>(*ops[0].w, seg, c, grid, stream, smem);
 }

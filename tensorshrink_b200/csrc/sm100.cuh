@@ -155,8 +155,11 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_by
 
 // Arrive on `bar` once all of this thread's prior cp.async copies have
 // landed (the barrier's expected count must include this arrival).
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+// Arrival on `bar` when this thread's prior cp.async copies complete; the
+// pending count is raised now and lowered by the completion, so the barrier's
+// expected count does not include these arrivals.
+__device__ __forceinline__ void cp_async_arrive_inc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
