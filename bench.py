@@ -52,8 +52,9 @@ METRIC = "QuantLinear packed-weight HBM GB/s (M=1) & TFLOP/s (M=2048); decode to
 HIDDEN, INTER = 4096, 14336
 # DRAM bytes per launch (read + write) measured by ncu on this workload
 QGEMV_TRAFFIC_BYTES = 31_679_488
-# the one-GPU step runs as one chained launch (see mlp_step)
-STEP_CHAIN = True
+# whether the timed one-GPU step runs as one persistent chained launch (see
+# mlp_step); measured slower than one launch per layer, so kept off
+STEP_CHAIN = False
 QGEMM_TRAFFIC_BYTES = 57_634_816 + 12_308_736
 
 
@@ -193,7 +194,7 @@ def chain_steps(blocks, x, per_block):
     return got
 
 
-def mlp_step(blocks, x, world=1, exchange=None, chain="step"):
+def mlp_step(blocks, x, world=1, exchange=None, chain=None):
     """One decode step through the MLP blocks. On one GPU the layers run as
     chained persistent launches (`chain`: "step" = one launch for every
     layer, "block" = one per block, None = one launch per layer). With
@@ -206,7 +207,7 @@ def mlp_step(blocks, x, world=1, exchange=None, chain="step"):
         from tensorshrink_b200.kernels import qlinear_chain
         groups, y = chain_steps(blocks, x, chain == "block")
         for g in groups:
-            qlinear_chain(g)
+            qlinear_chain(g, persistent=True)
         return y
     for gate_up, down in blocks:
         gu = gate_up(x)

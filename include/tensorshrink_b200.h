@@ -163,15 +163,17 @@ TS_API int ts_qlinear_ex(const ts_qlinear_op* op, int64_t M, void* workspace, si
 /*
  * A chain of n_ops layers where op i + 1 reads what op i wrote (an MLP:
  * gate_up then the gated down projection; or consecutive blocks). Results
- * equal n_ops ts_qlinear_ex calls in stream order. When every layer takes the
- * decode kernel in one pass with the same code layout (bits, group size,
- * codebook, double quant) and n_ops <= ts_qlinear_chain_max(), the chain is
- * ONE persistent launch: layer i + 1 waits (bounded) on a grid-wide counter
- * for layer i while the weight tiles of the following layers already stream
- * into shared memory. Otherwise the layers run as separate launches. The
- * workspace must cover ts_qlinear_workspace_size() of every layer.
+ * equal n_ops ts_qlinear_ex calls in stream order; every op is validated
+ * before any runs. persistent = 0: one decode launch per layer (each starts
+ * streaming its weights while the previous one finishes, by programmatic
+ * dependent launch). persistent != 0, when every layer takes the decode
+ * kernel in one pass with the same code layout (bits, group size, codebook,
+ * double quant) and n_ops <= ts_qlinear_chain_max(): ONE launch, in which
+ * layer i + 1 waits (bounded) on a grid-wide counter for layer i while the
+ * weight tiles of the following layers already stream into shared memory.
+ * The workspace must cover ts_qlinear_workspace_size() of every layer.
  */
-TS_API int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, void* workspace,
+TS_API int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, int persistent, void* workspace,
                             size_t workspace_bytes, void* stream);
 TS_API int ts_qlinear_chain_max(void);
 

@@ -87,7 +87,7 @@ _SIGNATURES = [
     ("ts_qlinear_gated", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int, _vp,
                                    C.c_int, _i64, _vp, C.c_size_t, _vp]),
     ("ts_qlinear_ex", C.c_int, [C.POINTER(TsQlinearOp), _i64, _vp, C.c_size_t, _vp]),
-    ("ts_qlinear_chain", C.c_int, [C.POINTER(TsQlinearOp), C.c_int, _i64, _vp, C.c_size_t, _vp]),
+    ("ts_qlinear_chain", C.c_int, [C.POINTER(TsQlinearOp), C.c_int, _i64, C.c_int, _vp, C.c_size_t, _vp]),
     ("ts_qlinear_chain_max", C.c_int, []),
     ("ts_qlinear_noalloc_max_scratch", C.c_size_t, []),
     ("ts_qlinear_noalloc", C.c_int, [C.POINTER(TsQWeight), _vp, C.c_int, _i64, _i64, _vp, C.c_int,

@@ -307,8 +307,8 @@ int ts_qlinear_ex(const ts_qlinear_op* o, int64_t M, void* workspace, size_t wor
 
 int ts_qlinear_chain_max(void) { return 8; }
 
-int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, void* workspace, size_t workspace_bytes,
-                     void* stream) {
+int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, int persistent, void* workspace,
+                     size_t workspace_bytes, void* stream) {
   TS_REQUIRE(ops != nullptr && n_ops >= 0, "bad op list");
   TS_REQUIRE(M >= 0, "M < 0");
   if (n_ops == 0 || M == 0) return TS_OK;
@@ -321,7 +321,7 @@ int ts_qlinear_chain(const ts_qlinear_op* ops, int n_ops, int64_t M, void* works
     TS_REQUIRE(ops[i].w->rows > 0, "empty layer in a chain");
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (n_ops > 1 && n_ops <= ts_qlinear_chain_max() && gemv_v1::gemv_chain_ok(g.data(), n_ops, M)) {
+  if (persistent && n_ops > 1 && n_ops <= ts_qlinear_chain_max() && gemv_v1::gemv_chain_ok(g.data(), n_ops, M)) {
     // the two-CTA-per-SM build when every layer fits it, else the one-CTA
     // one; TS_CHAIN_CTAS_PER_SM=1 selects the one-CTA build (tuning knob)
     const char* knob = getenv("TS_CHAIN_CTAS_PER_SM");

@@ -229,6 +229,17 @@ __device__ __forceinline__ uint32_t cta_of(uint64_t t, uint64_t U, uint64_t G) {
 // shared memory ahead of the stage ring: the ring's mbarriers and the CTA flags
 constexpr int kHeadBytes = 256;
 
+#ifdef TS_GEMV_PROF
+// Phase timings of an instrumented build (never the shipped library), per
+// CTA: [start clock, tile-loop start clock, cycles in full-stage waits, in
+// math, in flushes, tiles, producer cycles in empty-stage waits, end clock]
+// (consumer warp 0; clocks are per SM).
+__device__ unsigned long long g_gemv_prof[1024][8];
+#define TS_PROF(...) __VA_ARGS__
+#else
+#define TS_PROF(...)
+#endif
+
 // Waits (bounded) until every CTA of the launch has finished the previous
 // layer of a chain: consumer thread 0 polls the layer's counter, the other
 // consumer threads wait at the named barrier.
@@ -271,14 +282,15 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
   // per (token, segment): (activation scale, sum x, 0, 0)
   float4* sx = reinterpret_cast<float4*>(xb + a.mt * tok_stride);
   float* epi = reinterpret_cast<float*>(sx + a.mt * n_seg);
-  float* red = epi + a.max_owned_rows * kMaxTok;
-  int* o_ptr = reinterpret_cast<int*>(red + kConsumerWarps * kTileRows * kMaxTok);   // [owned rows + 1]
+  float* red = epi + a.max_owned_rows * kMaxTok;   // [stages][warps][kTileRows][mt] flush partials
+  int* o_ptr = reinterpret_cast<int*>(red + S * kConsumerWarps * kTileRows * a.mt);   // [owned rows + 1]
   int* o_col = o_ptr + a.max_owned_rows + 4;                                            // [kOutCap]
   uint32_t* o_dw = reinterpret_cast<uint32_t*>(o_col + kOutCap);   // [kOutCap / 2 + 1] fp16 deltas as words
   float* o_bias = reinterpret_cast<float*>(o_dw + kOutCap);                             // [owned rows]
   // set by the first wait that runs out: every role stops waiting and
   // unwinds (the producer first lets its copies in flight land)
   volatile int* s_abort = s_flag + 1;
+  int* s_cnt = s_flag + 4 + kMaxTok;   // [stages] flush arrivals per ring stage (zero between flushes)
   // per-stage metadata region (after the packed rows): plain: scale rows,
   // gmin rows; DQ: scale codes, gmin codes, scale supers, gmin supers
   const int mrw = a.meta_row_words;
@@ -301,10 +313,12 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
     uint32_t ph = rph;        // phase of the ring pass that stage s belongs to
     for (uint32_t i = 0; t0 + i < t1; ++i) {
       // warp-uniform decisions: every lane takes part in the __syncwarp below
+      TS_PROF(long long pf_e = clock64();)
       if (issued >= (uint32_t)S && !__all_sync(0xffffffffu, mbar_wait_hint(empty + s, ph ^ 1, a.err, 1, a.wait_ns))) {
         *s_abort = 1;
         break;
       }
+      TS_PROF(if (lane == 0) g_gemv_prof[blockIdx.x][6] += clock64() - pf_e;)
       if (__any_sync(0xffffffffu, *s_abort != 0)) break;
       char* st = stages + s * a.stage_bytes;
       uint32_t* meta = reinterpret_cast<uint32_t*>(st + kTileRows * kPitch);
@@ -464,9 +478,21 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
     for (int n = 0; n < kMaxTok; ++n) {
       if (n >= a.mt) break;
       const float* h = reinterpret_cast<const float*>(a.x) + (a.m0 + n) * a.x_stride;
-      for (int64_t k = threadIdx.x; k < C; k += kConsumerThreads) {
-        const float v = __ldcg(h + k);
-        ss[n] = fmaf(v, v, ss[n]);
+      if (a.x_vec16 && C % 4 == 0) {
+        const float4* h4 = reinterpret_cast<const float4*>(h);
+#pragma unroll 4
+        for (int64_t k = threadIdx.x; k < C / 4; k += kConsumerThreads) {
+          const float4 v = __ldcg(h4 + k);
+          ss[n] = fmaf(v.x, v.x, ss[n]);
+          ss[n] = fmaf(v.y, v.y, ss[n]);
+          ss[n] = fmaf(v.z, v.z, ss[n]);
+          ss[n] = fmaf(v.w, v.w, ss[n]);
+        }
+      } else {
+        for (int64_t k = threadIdx.x; k < C; k += kConsumerThreads) {
+          const float v = __ldcg(h + k);
+          ss[n] = fmaf(v, v, ss[n]);
+        }
       }
     }
     float* red0 = red;   // the flush scratch, free until the first flush
@@ -492,29 +518,57 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
     const int tps = seg_k / 16;                      // threads per segment (power of two)
     const uint32_t per_tok = (uint32_t)(a.q.padded_cols / 16);
     const uint32_t items = a.mt * per_tok;
-    for (uint32_t base = 0; base < items; base += kConsumerThreads) {
-      const uint32_t it = base + threadIdx.x;
+    // Each thread takes kU items per round and issues all their loads before
+    // converting any, so a round costs one L2 round trip (x was written by
+    // the previous kernel, or by this launch in a chain: L2-coherent loads).
+    constexpr int kU = 2;
+    for (uint32_t base0 = 0; base0 < items; base0 += kU * kConsumerThreads) {
+    uint4 raw[kU][4];
+#pragma unroll
+    for (int jr = 0; jr < kU; ++jr) {
+      const uint32_t it = base0 + jr * kConsumerThreads + threadIdx.x;
+      const bool live = it < items;
+      const uint32_t n = live ? it / per_tok : 0;
+      const uint32_t k0 = live ? (it - n * per_tok) * 16 : 0;
+      const int64_t xo = (a.m0 + n) * a.x_stride + k0;
+      if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
+        if (a.x_dtype == TS_F32) {
+          const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(a.x) + xo);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) raw[jr][c] = __ldcg(p + c);
+        } else {
+          const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + xo);
+          raw[jr][0] = __ldcg(p);
+          raw[jr][1] = __ldcg(p + 1);
+          if (a.gated) {
+            const uint4* pu = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + xo + a.q.cols);
+            raw[jr][2] = __ldcg(pu);
+            raw[jr][3] = __ldcg(pu + 1);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int jr = 0; jr < kU; ++jr) {
+      const uint32_t it = base0 + jr * kConsumerThreads + threadIdx.x;
       const bool live = it < items;
       const uint32_t n = live ? it / per_tok : 0;
       const uint32_t k0 = live ? (it - n * per_tok) * 16 : 0;
       const int64_t xo = (a.m0 + n) * a.x_stride + k0;
       float v[16];
-      // 16 activations at element offset `off` of the token's row
-      auto load16 = [&](int64_t off, float (&o)[16]) {
-        // (L2-coherent loads: in a chain x was written by this launch)
+      // 16 activations at element offset `off` of the token's row (part 1:
+      // the up half of a gated row)
+      auto load16 = [&](int64_t off, int part, float (&o)[16]) {
         if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols && a.x_dtype == TS_F32) {
-          const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + off);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float4 f = __ldcg(p + j);
-            o[4 * j] = f.x;
-            o[4 * j + 1] = f.y;
-            o[4 * j + 2] = f.z;
-            o[4 * j + 3] = f.w;
+            o[4 * j] = __uint_as_float(raw[jr][j].x);
+            o[4 * j + 1] = __uint_as_float(raw[jr][j].y);
+            o[4 * j + 2] = __uint_as_float(raw[jr][j].z);
+            o[4 * j + 3] = __uint_as_float(raw[jr][j].w);
           }
         } else if (live && a.x_vec16 && k0 + 16 <= (uint32_t)a.q.cols) {
-          const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + off);
-          const uint4 r0 = __ldcg(p), r1 = __ldcg(p + 1);
+          const uint4 r0 = raw[jr][2 * part], r1 = raw[jr][2 * part + 1];
           const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -533,13 +587,13 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
             o[j] = (live && k0 + j < (uint32_t)a.q.cols) ? load_f_cg(a.x, a.x_dtype, off + j) : 0.f;
         }
       };
-      load16(xo, v);
+      load16(xo, 0, v);
       if (a.gated) {
         // gated MLP input: x = silu(gate) * up with gate, up the two halves of
         // the row, each rounded to the activation dtype as the unfused
         // F.silu(gate) * up would round them
         float u[16];
-        load16(xo + a.q.cols, u);
+        load16(xo + a.q.cols, 1, u);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const float sl = round_act(v[j] / (1.f + __expf(-v[j])), a.act_dtype);
@@ -654,6 +708,7 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
         }
       }
     }
+    }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   named_bar_sync(1, kConsumerThreads);
@@ -743,8 +798,10 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
 
   int& cs = rs;          // consumers: the ring position carries over between layers
   uint32_t& cph = rph;
+  TS_PROF(long long pf_wait = 0, pf_math = 0, pf_flush = 0; long long pf_t = clock64();)
   for (uint32_t i = 0; t0 + i < t1; ++i) {
     const int s = cs;
+    TS_PROF(long long pf_a = clock64();)
     // warp-uniform: the MMAs below need every lane; after any role's timeout
     // the remaining tiles are skipped without waiting
     bool ok = !__any_sync(0xffffffffu, *s_abort != 0);
@@ -753,6 +810,7 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
       *s_abort = 1;
     }
     if (++cs == S) { cs = 0; cph ^= 1; }
+    TS_PROF(long long pf_b = clock64(); pf_wait += pf_b - pf_a;)
     const char* st = stages + s * a.stage_bytes;
     const uint32_t* meta = reinterpret_cast<const uint32_t*>(st + kTileRows * kPitch);
     const uint32_t g0 = kg * (uint32_t)a.gpt;
@@ -868,7 +926,7 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
         for (int sg = 0; sg < NSG; ++sg) {
           va[0][sg] = va[1][sg] = 0;
           if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) continue;
-          int c4[4] = {0, 0, 0, 0};
+          int c4[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};   // two independent MMA chains
 #pragma unroll
           for (int cj = 0; cj < SEG; ++cj) {
             const int cb = (sg * SEG + cj) * 16;
@@ -880,11 +938,11 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
               int J;
               unpack(w0, w1, ch_slice + sg * SEG + cj, m, A0, A1, A2, A3, J);
               const uint2 b0 = has_b0 ? xi_lane0[J * xcols * 4] : make_uint2(0u, 0u);
-              imma16832(c4, A0, A1, A2, A3, b0.x, b0.y);
+              imma16832(c4[(cj * NM + m) & 1], A0, A1, A2, A3, b0.x, b0.y);
             }
           }
-          va[0][sg] = 256 * c4[0] + c4[1];
-          va[1][sg] = 256 * c4[2] + c4[3];
+          va[0][sg] = 256 * (c4[0][0] + c4[1][0]) + (c4[0][1] + c4[1][1]);
+          va[1][sg] = 256 * (c4[0][2] + c4[1][2]) + (c4[0][3] + c4[1][3]);
         }
 #pragma unroll
         for (int s0 = 0; s0 < NSG; s0 += 4) {
@@ -958,79 +1016,123 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty + s);
+    TS_PROF(long long pf_c = clock64(); pf_math += pf_c - pf_b;)
 
     const bool last_kg = kg == KG - 1;
-    if (last_kg || t0 + i + 1 == t1) {
-      // ---- flush row block rb: reduce the 8 warps' k-slices through smem ----
-      float* rw = red + warp * kTileRows * kMaxTok;
+    if (!(last_kg || t0 + i + 1 == t1)) {
+      if (lane == 0) mbar_arrive(empty + s);
+    } else {
+      // ---- flush row block rb: each warp leaves its k-slice partials in the
+      // stage's reduction slot; the last warp to arrive (shared counter) sums
+      // them in warp order and finishes the row block while the other warps
+      // go on with the next tiles. Every warp releases the stage only after
+      // its part, so the slot is not reused before the reduction is done.
+      const int mt = a.mt;
+      float* rslot = red + (size_t)s * kConsumerWarps * kTileRows * mt;
+      float* rw = rslot + warp * kTileRows * mt;
       if constexpr (CB) {
-        rw[q * kMaxTok + 2 * l] = acc[0];
-        rw[q * kMaxTok + 2 * l + 1] = acc[1];
-        rw[(q + 8) * kMaxTok + 2 * l] = acc[2];
-        rw[(q + 8) * kMaxTok + 2 * l + 1] = acc[3];
+        if (2 * l < mt) {
+          rw[q * mt + 2 * l] = acc[0];
+          rw[(q + 8) * mt + 2 * l] = acc[2];
+        }
+        if (2 * l + 1 < mt) {
+          rw[q * mt + 2 * l + 1] = acc[1];
+          rw[(q + 8) * mt + 2 * l + 1] = acc[3];
+        }
       } else {
-        if (a.mt == 1) {   // the four lanes of a row pair hold partials of token 0
+        if (mt == 1) {   // the four lanes of a row pair hold partials of token 0
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
             acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
             acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
           }
         }
-        rw[q * kMaxTok + l] = acc[0];
-        rw[(q + 8) * kMaxTok + l] = acc[1];
-        rw[q * kMaxTok + 4 + l] = acc[2];
-        rw[(q + 8) * kMaxTok + 4 + l] = acc[3];
+        if (l < mt && (mt > 1 || l == 0)) {
+          rw[q * mt + l] = acc[0];
+          rw[(q + 8) * mt + l] = acc[1];
+        }
+        if (4 + l < mt) {
+          rw[q * mt + 4 + l] = acc[2];
+          rw[(q + 8) * mt + 4 + l] = acc[3];
+        }
       }
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-      named_bar_sync(1, kConsumerThreads);
-      const int t = threadIdx.x;                 // t < 128: (row t/8, token t%8)
-      const int rr = t >> 3, n = t & 7;
-      const int64_t row = (int64_t)rb * kTileRows + rr;
-      float tot = 0.f;
-      if (t < kTileRows * kMaxTok) {
-        for (int w = 0; w < kConsumerWarps; ++w) tot += red[(w * kTileRows + rr) * kMaxTok + n];
-        if (started_here) tot += epi[((rb - rb_own0) * kTileRows + rr) * kMaxTok + n];
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(s_cnt + s, 1) == kConsumerWarps - 1;
       }
-      if (started_here && last_kg) {
-        if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
-          store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
-                  a.residual ? tot + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : tot);
-      } else {
-        const int slot = rb == first_rb ? 0 : 1;
-        if (t < kTileRows * kMaxTok)
-          a.partials[((size_t)blockIdx.x * 2 + slot) * (kTileRows * kMaxTok) + t] = tot;
-        __threadfence();
-        named_bar_sync(1, kConsumerThreads);
-        if (t == 0) *s_flag = atomicAdd(a.counters + rb, 1);
-        named_bar_sync(1, kConsumerThreads);
-        const int old = *s_flag;
-        const uint64_t u0 = (uint64_t)rb * KG;
-        int pieces = 1;
-        for (uint32_t cc = 1, prev = cta_of(u0 / Q, UQ, GR); cc < KG; ++cc) {
-          const uint32_t w = cta_of((u0 + cc) / Q, UQ, GR);
-          pieces += w != prev;
-          prev = w;
-        }
-        if (old == pieces - 1) {
-          __threadfence();
-          float sum = 0.f;
-          for (uint32_t cc = 0, prev = 0xFFFFFFFFu; cc < KG; ++cc) {
-            const uint32_t pc = cta_of((u0 + cc) / Q, UQ, GR);
-            if (pc == prev) continue;
-            prev = pc;
-            const uint32_t pfirst = (uint32_t)((UQ * pc / GR * Q) / KG);
-            if (t < kTileRows * kMaxTok)
-              sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) + t);
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence_block();
+        const int n_pairs = kTileRows * mt;   // (row, token) pairs, <= 128
+        const bool direct = started_here && last_kg;
+        float tot[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = lane + 32 * u;
+          tot[u] = 0.f;
+          if (j < n_pairs) {
+            for (int w = 0; w < kConsumerWarps; ++w) tot[u] += rslot[w * kTileRows * mt + j];
+            const int rr = j / mt, n = j - rr * mt;
+            if (started_here) tot[u] += epi[((rb - rb_own0) * kTileRows + rr) * kMaxTok + n];
+            const int64_t row = (int64_t)rb * kTileRows + rr;
+            if (direct) {
+              if (row < a.q.rows)
+                store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
+                        a.residual ? tot[u] + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : tot[u]);
+            } else {
+              const int slot = rb == first_rb ? 0 : 1;
+              a.partials[((size_t)blockIdx.x * 2 + slot) * (kTileRows * kMaxTok) + rr * kMaxTok + n] = tot[u];
+            }
           }
-          if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
-            store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
-                    a.residual ? sum + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : sum);
-          if (t == 0) a.counters[rb] = 0;
         }
+        if (!direct) {
+          // a row block split between CTAs: the last CTA to arrive (global
+          // counter) adds the pieces' partials in CTA order
+          __threadfence();
+          __syncwarp();
+          int old = 0;
+          if (lane == 0) old = atomicAdd(a.counters + rb, 1);
+          old = __shfl_sync(0xffffffffu, old, 0);
+          const uint64_t u0 = (uint64_t)rb * KG;
+          int pieces = 1;
+          for (uint32_t cc = 1, prev = cta_of(u0 / Q, UQ, GR); cc < KG; ++cc) {
+            const uint32_t w = cta_of((u0 + cc) / Q, UQ, GR);
+            pieces += w != prev;
+            prev = w;
+          }
+          if (old == pieces - 1) {
+            __threadfence();
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int j = lane + 32 * u;
+              if (j >= n_pairs) continue;
+              const int rr = j / mt, n = j - rr * mt;
+              float sum = 0.f;
+              for (uint32_t cc = 0, prev = 0xFFFFFFFFu; cc < KG; ++cc) {
+                const uint32_t pc = cta_of((u0 + cc) / Q, UQ, GR);
+                if (pc == prev) continue;
+                prev = pc;
+                const uint32_t pfirst = (uint32_t)((UQ * pc / GR * Q) / KG);
+                sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) +
+                              rr * kMaxTok + n);
+              }
+              const int64_t row = (int64_t)rb * kTileRows + rr;
+              if (row < a.q.rows)
+                store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
+                        a.residual ? sum + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : sum);
+            }
+            if (lane == 0) a.counters[rb] = 0;
+          }
+        }
+        if (lane == 0) s_cnt[s] = 0;
+        __syncwarp();
       }
-      named_bar_sync(1, kConsumerThreads);  // `red` and `s_flag` are reused by the next flush
+      if (lane == 0) mbar_arrive(empty + s);
     }
+    TS_PROF(pf_flush += clock64() - pf_c;)
     if (last_kg) {
       kg = 0;
       ++rb;
@@ -1039,6 +1141,15 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
       ++kg;
     }
   }
+  TS_PROF(if (threadIdx.x == 0) {
+    unsigned long long* pr = g_gemv_prof[blockIdx.x];   // consumer warp 0, lane 0
+    if (layer == 0) pr[1] = (unsigned long long)pf_t;
+    pr[2] += pf_wait;
+    pr[3] += pf_math;
+    pr[4] += pf_flush;
+    pr[5] += t1 - t0;
+    pr[7] = (unsigned long long)clock64();
+  })
 }
 
 template <int BITS, bool CB, bool DQ, int SEG, int NL>
@@ -1050,6 +1161,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const __gri
   float* s_rstd = reinterpret_cast<float*>(s_flag + 4);        // [kMaxTok] RMSNorm factors
   char* body = smem + kHeadBytes;
   const Args& a0 = c.L[0];
+  TS_PROF(if (threadIdx.x == 0) {
+    for (int k = 1; k < 8; ++k) g_gemv_prof[blockIdx.x][k] = 0;
+    g_gemv_prof[blockIdx.x][0] = (unsigned long long)clock64();
+  })
   const int S = a0.stages;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -1057,6 +1172,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const __gri
       mbar_init(empty + i, kConsumerWarps);
     }
     s_flag[1] = 0;
+    for (int i = 0; i < kMaxStages; ++i) s_flag[4 + kMaxTok + i] = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -1181,17 +1297,19 @@ size_t fixed_smem(const ts_qweight& w, const Plan& p, int mt) {
   const size_t n_seg = (size_t)p.n_chunks / p.seg_chunks;
   return lut_bytes(w) + (size_t)mt * (n_mma * 4 + 4) * 8 + (size_t)mt * n_seg * 16 +
          (size_t)p.max_owned_rows * gemv::kMaxTok * 4 +
-         (size_t)gemv::kConsumerWarps * gemv::kTileRows * gemv::kMaxTok * 4 +
          (size_t)(p.max_owned_rows + 4) * 4 + (size_t)gemv::kOutCap * 8 + (size_t)(p.max_owned_rows + 4) * 4 +
          gemv::kHeadBytes + 64;
 }
+
+// shared memory per ring stage besides the stage itself: its flush slot
+size_t red_bytes(int mt) { return (size_t)gemv::kConsumerWarps * gemv::kTileRows * mt * 4; }
 
 size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024 / gemv::kCtasPerSm - (gemv::kCtasPerSm - 1) * 1024); }
 
 int stages_for(const ts_qweight& w, const Plan& p, int mt) {
   const size_t f = fixed_smem(w, p, mt);
   if (f >= smem_cap()) return 0;
-  return (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - f) / p.stage_bytes);
+  return (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - f) / (p.stage_bytes + red_bytes(mt)));
 }
 
 template <int BITS, bool CB, bool DQ, int SEG, int NL>
@@ -1384,7 +1502,7 @@ int run_gemv(const GemvOp& op, int64_t M, void* workspace, size_t ws_bytes, cuda
     a.m0 = m0;
     a.mt = (int)std::min<int64_t>(max_mt, M - m0);
     a.stages = stages_for(w, p, a.mt);
-    const size_t smem = fixed_smem(w, p, a.mt) + (size_t)a.stages * p.stage_bytes;
+    const size_t smem = fixed_smem(w, p, a.mt) + (size_t)a.stages * (p.stage_bytes + red_bytes(a.mt));
     rc = launch_chain<1>(w, p.seg_chunks, c, p.grid, stream, smem);
     if (rc != TS_OK) return rc;
   }
@@ -1434,16 +1552,29 @@ int run_gemv_chain(const GemvOp* ops, int n, int64_t M, void* workspace, size_t 
     stage_bytes = std::max(stage_bytes, p.stage_bytes);   // rows first, then the layer's metadata
   }
   TS_UNSUPPORTED(fixed < smem_cap(), "qlinear chain: shared memory");
-  stages = (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - fixed) / stage_bytes);
+  stages = (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - fixed) / (stage_bytes + red_bytes((int)M)));
   TS_UNSUPPORTED(stages >= 2, "qlinear chain: shared memory for two stages");
   c.L[0].stall = take_test_stall() ? 1 : 0;
   for (int i = 0; i < n; ++i) {
     c.L[i].stages = stages;
     c.L[i].stage_bytes = stage_bytes;
   }
-  const size_t smem = fixed + (size_t)stages * stage_bytes;
+  const size_t smem = fixed + (size_t)stages * (stage_bytes + red_bytes((int)M));
   return launch_chain<gemv::kMaxChain>(*ops[0].w, seg, c, grid, stream, smem);
 }
 
+#ifdef TS_GEMV_PROF
+int gemv_prof_read(void* dst) {
+  TS_CUDA_TRY(cudaMemcpyFromSymbol(dst, gemv::g_gemv_prof, sizeof(gemv::g_gemv_prof)));
+  return TS_OK;
+}
+#endif
+
 }  // namespace TS_GEMV_NS
 }  // namespace ts
+
+#ifdef TS_GEMV_PROF
+#define TS_PROF_CAT2(a, b) a##b
+#define TS_PROF_CAT(a, b) TS_PROF_CAT2(a, b)
+extern "C" __attribute__((visibility("default"))) int TS_PROF_CAT(ts_prof_read_, TS_GEMV_NS)(void* dst) { return ts::TS_GEMV_NS::gemv_prof_read(dst); }
+#endif

@@ -153,8 +153,6 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_by
                : "memory");
 }
 
-// Arrive on `bar` once all of this thread's prior cp.async copies have
-// landed (the barrier's expected count must include this arrival).
 // Arrival on `bar` when this thread's prior cp.async copies complete; the
 // pending count is raised now and lowered by the completion, so the barrier's
 // expected count does not include these arrivals.

@@ -305,11 +305,12 @@ class ChainStep:
             self.out.copy_(self.residual + y)
 
 
-def qlinear_chain(steps: List[ChainStep]) -> None:
+def qlinear_chain(steps: List[ChainStep], persistent: bool = False) -> None:
     """Run `steps` in order (step i + 1 may read what step i wrote) through
-    `ts_qlinear_chain`: for decode-sized M one persistent launch when the
-    layers share a code layout, else one decode launch each; calls the decode
-    kernel does not take run unfused, step by step."""
+    `ts_qlinear_chain`: decode-sized calls as one decode launch per step, or
+    with `persistent` as one launch over every step when the layers share a
+    code layout; calls the decode kernel does not take run unfused, step by
+    step."""
     if not steps:
         return
     lib = _C.load()
@@ -320,7 +321,8 @@ def qlinear_chain(steps: List[ChainStep]) -> None:
     need = max(int(lib.ts_qlinear_workspace_size(st.qw, M)) for st in steps)
     ws = workspace_for(dev, need)
     arr = (_C.TsQlinearOp * len(steps))(*[st.to_c() for st in steps])
-    rc = lib.ts_qlinear_chain(arr, len(steps), M, ws.data_ptr(), int(ws.numel()), _stream_handle(dev))
+    rc = lib.ts_qlinear_chain(arr, len(steps), M, 1 if persistent else 0, ws.data_ptr(), int(ws.numel()),
+                              _stream_handle(dev))
     if rc == -2:      # validated before anything ran: run the layers unfused
         for st in steps:
             st.run_unfused()

@@ -64,7 +64,7 @@ def test_chain_equals_separate_launches(blocks, M, n_blocks):
     outs = [(torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16),
              torch.empty(M, H, device="cuda", dtype=torch.bfloat16)) for _ in bl]
     before = kernels._C.load().ts_launch_count(1)
-    kernels.qlinear_chain(_chain_steps(bl, x, outs))
+    kernels.qlinear_chain(_chain_steps(bl, x, outs), persistent=True)
     launches = kernels._C.load().ts_launch_count(1)
     assert launches == 1, f"a chain of {2 * n_blocks} layers took {launches} launches"
     del before
@@ -82,19 +82,21 @@ def test_chain_repeats_and_replays_in_a_graph(blocks):
     outs = [(torch.empty(1, 2 * I, device="cuda", dtype=torch.bfloat16),
              torch.empty(1, H, device="cuda", dtype=torch.bfloat16)) for _ in blocks]
     steps = _chain_steps(blocks, x, outs)
-    kernels.qlinear_chain(steps)
+    kernels.qlinear_chain(steps, persistent=True)
     first = outs[-1][1].clone()
     for _ in range(3):
-        kernels.qlinear_chain(steps)
+        kernels.qlinear_chain(steps, persistent=True)
         assert torch.equal(outs[-1][1], first)
+    kernels.qlinear_chain(steps)            # one launch per layer: the same result
+    assert torch.equal(outs[-1][1], first)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        kernels.qlinear_chain(steps)
+        kernels.qlinear_chain(steps, persistent=True)
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        kernels.qlinear_chain(steps)
+        kernels.qlinear_chain(steps, persistent=True)
     for _ in range(5):
         outs[-1][1].zero_()
         g.replay()
@@ -114,7 +116,7 @@ def test_chain_of_mixed_layouts_runs_layer_by_layer():
     t = torch.empty(3, 768, device="cuda", dtype=torch.float16)
     y = torch.empty(3, H, device="cuda", dtype=torch.float16)
     kernels._C.load().ts_launch_count(1)
-    kernels.qlinear_chain([ChainStep(a.qweight(), x, t), ChainStep(b.qweight(), t, y)])
+    kernels.qlinear_chain([ChainStep(a.qweight(), x, t), ChainStep(b.qweight(), t, y)], persistent=True)
     assert kernels._C.load().ts_launch_count(1) == 2
     ref = kernels.qlinear(kernels.qlinear(x, a.qweight(), None, torch.float16), b.qweight(), None, torch.float16)
     assert torch.equal(y, ref)
@@ -181,11 +183,11 @@ def test_chain_wait_timeout_is_reported(blocks):
              torch.empty(1, H, device="cuda", dtype=torch.bfloat16)) for _ in blocks[:2]]
     steps = _chain_steps(blocks[:2], x, outs)
     _C.check(lib.ts_test_inject_stall(20_000_000), "stall")
-    kernels.qlinear_chain(steps)
+    kernels.qlinear_chain(steps, persistent=True)
     torch.cuda.synchronize()
     with pytest.raises(RuntimeError, match="bounded wait"):
         kernels.device_status()
-    kernels.qlinear_chain(steps)
+    kernels.qlinear_chain(steps, persistent=True)
     torch.cuda.synchronize()
     kernels.device_status()
     assert torch.equal(outs[-1][1], _sequential(blocks[:2], x))
