@@ -1003,8 +1003,9 @@ def main():
                                                        "library's one-shot all-reduce kernel")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="--impl reference: skip the reference's own CUDA/Triton timing")
-    ap.add_argument("--only", choices=("decoder",), default=None,
-                    help="run one study alone (short; for launch lists): the 8B decoder at batch 1")
+    ap.add_argument("--only", choices=("decoder", "quantize", "prefill"), default=None,
+                    help="run one study alone (short; for launch lists and profiles): the 8B decoder at "
+                         "batch 1, the [28672, 8192] quantize, or the config-3 prefill layer")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()
@@ -1038,6 +1039,12 @@ def main():
         out = decoder_measure(device, world, timed_only, batches=(1,), steps=args.steps, prefill=False)
         if rank == 0:
             print(json.dumps(out), flush=True)
+        return
+    if args.only == "quantize":
+        print(json.dumps(quantize_measure(device, reps=max(1, args.steps))), flush=True)
+        return
+    if args.only == "prefill":
+        print(json.dumps(prefill_measure(device, reps=max(1, args.steps))), flush=True)
         return
     out = run_ours(args, rank, world, device)
     if rank == 0:

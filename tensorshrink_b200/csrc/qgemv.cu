@@ -282,15 +282,14 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
   // per (token, segment): (activation scale, sum x, 0, 0)
   float4* sx = reinterpret_cast<float4*>(xb + a.mt * tok_stride);
   float* epi = reinterpret_cast<float*>(sx + a.mt * n_seg);
-  float* red = epi + a.max_owned_rows * kMaxTok;   // [stages][warps][kTileRows][mt] flush partials
-  int* o_ptr = reinterpret_cast<int*>(red + S * kConsumerWarps * kTileRows * a.mt);   // [owned rows + 1]
+  float* red = epi + a.max_owned_rows * kMaxTok;
+  int* o_ptr = reinterpret_cast<int*>(red + kConsumerWarps * kTileRows * kMaxTok);   // [owned rows + 1]
   int* o_col = o_ptr + a.max_owned_rows + 4;                                            // [kOutCap]
   uint32_t* o_dw = reinterpret_cast<uint32_t*>(o_col + kOutCap);   // [kOutCap / 2 + 1] fp16 deltas as words
   float* o_bias = reinterpret_cast<float*>(o_dw + kOutCap);                             // [owned rows]
   // set by the first wait that runs out: every role stops waiting and
   // unwinds (the producer first lets its copies in flight land)
   volatile int* s_abort = s_flag + 1;
-  int* s_cnt = s_flag + 4 + kMaxTok;   // [stages] flush arrivals per ring stage (zero between flushes)
   // per-stage metadata region (after the packed rows): plain: scale rows,
   // gmin rows; DQ: scale codes, gmin codes, scale supers, gmin supers
   const int mrw = a.meta_row_words;
@@ -518,10 +517,10 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
     const int tps = seg_k / 16;                      // threads per segment (power of two)
     const uint32_t per_tok = (uint32_t)(a.q.padded_cols / 16);
     const uint32_t items = a.mt * per_tok;
-    // Each thread takes kU items per round and issues all their loads before
-    // converting any, so a round costs one L2 round trip (x was written by
-    // the previous kernel, or by this launch in a chain: L2-coherent loads).
-    constexpr int kU = 2;
+    // kU items per thread per round, loads first (one item measured fastest:
+    // more raise register pressure); x was written by the previous kernel,
+    // or by this launch in a chain, so the loads are L2-coherent
+    constexpr int kU = 1;
     for (uint32_t base0 = 0; base0 < items; base0 += kU * kConsumerThreads) {
     uint4 raw[kU][4];
 #pragma unroll
@@ -596,7 +595,7 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
         load16(xo + a.q.cols, 1, u);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const float sl = round_act(v[j] / (1.f + __expf(-v[j])), a.act_dtype);
+          const float sl = round_act(__fdividef(v[j], 1.f + __expf(-v[j])), a.act_dtype);
           v[j] = round_act(sl * u[j], a.act_dtype);
         }
       } else if (a.norm_w) {
@@ -926,7 +925,7 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
         for (int sg = 0; sg < NSG; ++sg) {
           va[0][sg] = va[1][sg] = 0;
           if (!ok || slice_byte0 + sg * SEG * 16 >= (uint32_t)a.q.row_bytes) continue;
-          int c4[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};   // two independent MMA chains
+          int c4[4] = {0, 0, 0, 0};
 #pragma unroll
           for (int cj = 0; cj < SEG; ++cj) {
             const int cb = (sg * SEG + cj) * 16;
@@ -938,11 +937,11 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
               int J;
               unpack(w0, w1, ch_slice + sg * SEG + cj, m, A0, A1, A2, A3, J);
               const uint2 b0 = has_b0 ? xi_lane0[J * xcols * 4] : make_uint2(0u, 0u);
-              imma16832(c4[(cj * NM + m) & 1], A0, A1, A2, A3, b0.x, b0.y);
+              imma16832(c4, A0, A1, A2, A3, b0.x, b0.y);
             }
           }
-          va[0][sg] = 256 * (c4[0][0] + c4[1][0]) + (c4[0][1] + c4[1][1]);
-          va[1][sg] = 256 * (c4[0][2] + c4[1][2]) + (c4[0][3] + c4[1][3]);
+          va[0][sg] = 256 * c4[0] + c4[1];
+          va[1][sg] = 256 * c4[2] + c4[3];
         }
 #pragma unroll
         for (int s0 = 0; s0 < NSG; s0 += 4) {
@@ -1016,121 +1015,79 @@ __device__ __forceinline__ void gemv_layer(const Args& a, char* smem, uint64_t* 
       }
     }
     __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
     TS_PROF(long long pf_c = clock64(); pf_math += pf_c - pf_b;)
 
     const bool last_kg = kg == KG - 1;
-    if (!(last_kg || t0 + i + 1 == t1)) {
-      if (lane == 0) mbar_arrive(empty + s);
-    } else {
-      // ---- flush row block rb: each warp leaves its k-slice partials in the
-      // stage's reduction slot; the last warp to arrive (shared counter) sums
-      // them in warp order and finishes the row block while the other warps
-      // go on with the next tiles. Every warp releases the stage only after
-      // its part, so the slot is not reused before the reduction is done.
-      const int mt = a.mt;
-      float* rslot = red + (size_t)s * kConsumerWarps * kTileRows * mt;
-      float* rw = rslot + warp * kTileRows * mt;
+    if (last_kg || t0 + i + 1 == t1) {
+      // ---- flush row block rb: reduce the 8 warps' k-slices through smem ----
+      float* rw = red + warp * kTileRows * kMaxTok;
       if constexpr (CB) {
-        if (2 * l < mt) {
-          rw[q * mt + 2 * l] = acc[0];
-          rw[(q + 8) * mt + 2 * l] = acc[2];
-        }
-        if (2 * l + 1 < mt) {
-          rw[q * mt + 2 * l + 1] = acc[1];
-          rw[(q + 8) * mt + 2 * l + 1] = acc[3];
-        }
+        rw[q * kMaxTok + 2 * l] = acc[0];
+        rw[q * kMaxTok + 2 * l + 1] = acc[1];
+        rw[(q + 8) * kMaxTok + 2 * l] = acc[2];
+        rw[(q + 8) * kMaxTok + 2 * l + 1] = acc[3];
       } else {
-        if (mt == 1) {   // the four lanes of a row pair hold partials of token 0
+        if (a.mt == 1) {   // the four lanes of a row pair hold partials of token 0
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
             acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
             acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
           }
         }
-        if (l < mt && (mt > 1 || l == 0)) {
-          rw[q * mt + l] = acc[0];
-          rw[(q + 8) * mt + l] = acc[1];
-        }
-        if (4 + l < mt) {
-          rw[q * mt + 4 + l] = acc[2];
-          rw[(q + 8) * mt + 4 + l] = acc[3];
-        }
+        rw[q * kMaxTok + l] = acc[0];
+        rw[(q + 8) * kMaxTok + l] = acc[1];
+        rw[q * kMaxTok + 4 + l] = acc[2];
+        rw[(q + 8) * kMaxTok + 4 + l] = acc[3];
       }
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) {
-        __threadfence_block();
-        last = atomicAdd(s_cnt + s, 1) == kConsumerWarps - 1;
+      named_bar_sync(1, kConsumerThreads);
+      const int t = threadIdx.x;                 // t < 128: (row t/8, token t%8)
+      const int rr = t >> 3, n = t & 7;
+      const int64_t row = (int64_t)rb * kTileRows + rr;
+      float tot = 0.f;
+      if (t < kTileRows * kMaxTok) {
+        for (int w = 0; w < kConsumerWarps; ++w) tot += red[(w * kTileRows + rr) * kMaxTok + n];
+        if (started_here) tot += epi[((rb - rb_own0) * kTileRows + rr) * kMaxTok + n];
       }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence_block();
-        const int n_pairs = kTileRows * mt;   // (row, token) pairs, <= 128
-        const bool direct = started_here && last_kg;
-        float tot[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = lane + 32 * u;
-          tot[u] = 0.f;
-          if (j < n_pairs) {
-            for (int w = 0; w < kConsumerWarps; ++w) tot[u] += rslot[w * kTileRows * mt + j];
-            const int rr = j / mt, n = j - rr * mt;
-            if (started_here) tot[u] += epi[((rb - rb_own0) * kTileRows + rr) * kMaxTok + n];
-            const int64_t row = (int64_t)rb * kTileRows + rr;
-            if (direct) {
-              if (row < a.q.rows)
-                store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
-                        a.residual ? tot[u] + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : tot[u]);
-            } else {
-              const int slot = rb == first_rb ? 0 : 1;
-              a.partials[((size_t)blockIdx.x * 2 + slot) * (kTileRows * kMaxTok) + rr * kMaxTok + n] = tot[u];
-            }
-          }
+      if (started_here && last_kg) {
+        if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
+          store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
+                  a.residual ? tot + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : tot);
+      } else {
+        const int slot = rb == first_rb ? 0 : 1;
+        if (t < kTileRows * kMaxTok)
+          a.partials[((size_t)blockIdx.x * 2 + slot) * (kTileRows * kMaxTok) + t] = tot;
+        __threadfence();
+        named_bar_sync(1, kConsumerThreads);
+        if (t == 0) *s_flag = atomicAdd(a.counters + rb, 1);
+        named_bar_sync(1, kConsumerThreads);
+        const int old = *s_flag;
+        const uint64_t u0 = (uint64_t)rb * KG;
+        int pieces = 1;
+        for (uint32_t cc = 1, prev = cta_of(u0 / Q, UQ, GR); cc < KG; ++cc) {
+          const uint32_t w = cta_of((u0 + cc) / Q, UQ, GR);
+          pieces += w != prev;
+          prev = w;
         }
-        if (!direct) {
-          // a row block split between CTAs: the last CTA to arrive (global
-          // counter) adds the pieces' partials in CTA order
+        if (old == pieces - 1) {
           __threadfence();
-          __syncwarp();
-          int old = 0;
-          if (lane == 0) old = atomicAdd(a.counters + rb, 1);
-          old = __shfl_sync(0xffffffffu, old, 0);
-          const uint64_t u0 = (uint64_t)rb * KG;
-          int pieces = 1;
-          for (uint32_t cc = 1, prev = cta_of(u0 / Q, UQ, GR); cc < KG; ++cc) {
-            const uint32_t w = cta_of((u0 + cc) / Q, UQ, GR);
-            pieces += w != prev;
-            prev = w;
+          float sum = 0.f;
+          for (uint32_t cc = 0, prev = 0xFFFFFFFFu; cc < KG; ++cc) {
+            const uint32_t pc = cta_of((u0 + cc) / Q, UQ, GR);
+            if (pc == prev) continue;
+            prev = pc;
+            const uint32_t pfirst = (uint32_t)((UQ * pc / GR * Q) / KG);
+            if (t < kTileRows * kMaxTok)
+              sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) + t);
           }
-          if (old == pieces - 1) {
-            __threadfence();
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int j = lane + 32 * u;
-              if (j >= n_pairs) continue;
-              const int rr = j / mt, n = j - rr * mt;
-              float sum = 0.f;
-              for (uint32_t cc = 0, prev = 0xFFFFFFFFu; cc < KG; ++cc) {
-                const uint32_t pc = cta_of((u0 + cc) / Q, UQ, GR);
-                if (pc == prev) continue;
-                prev = pc;
-                const uint32_t pfirst = (uint32_t)((UQ * pc / GR * Q) / KG);
-                sum += __ldcg(a.partials + ((size_t)pc * 2 + (rb == pfirst ? 0 : 1)) * (kTileRows * kMaxTok) +
-                              rr * kMaxTok + n);
-              }
-              const int64_t row = (int64_t)rb * kTileRows + rr;
-              if (row < a.q.rows)
-                store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
-                        a.residual ? sum + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : sum);
-            }
-            if (lane == 0) a.counters[rb] = 0;
-          }
+          if (t < kTileRows * kMaxTok && n < a.mt && row < a.q.rows)
+            store_f(a.out, a.out_dtype, (a.m0 + n) * a.out_stride + row,
+                    a.residual ? sum + __ldcg(a.residual + (a.m0 + n) * a.residual_stride + row) : sum);
+          if (t == 0) a.counters[rb] = 0;
         }
-        if (lane == 0) s_cnt[s] = 0;
-        __syncwarp();
       }
-      if (lane == 0) mbar_arrive(empty + s);
+      named_bar_sync(1, kConsumerThreads);  // `red` and `s_flag` are reused by the next flush
     }
     TS_PROF(pf_flush += clock64() - pf_c;)
     if (last_kg) {
@@ -1172,7 +1129,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qgemv_kernel(const __gri
       mbar_init(empty + i, kConsumerWarps);
     }
     s_flag[1] = 0;
-    for (int i = 0; i < kMaxStages; ++i) s_flag[4 + kMaxTok + i] = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -1297,19 +1253,17 @@ size_t fixed_smem(const ts_qweight& w, const Plan& p, int mt) {
   const size_t n_seg = (size_t)p.n_chunks / p.seg_chunks;
   return lut_bytes(w) + (size_t)mt * (n_mma * 4 + 4) * 8 + (size_t)mt * n_seg * 16 +
          (size_t)p.max_owned_rows * gemv::kMaxTok * 4 +
+         (size_t)gemv::kConsumerWarps * gemv::kTileRows * gemv::kMaxTok * 4 +
          (size_t)(p.max_owned_rows + 4) * 4 + (size_t)gemv::kOutCap * 8 + (size_t)(p.max_owned_rows + 4) * 4 +
          gemv::kHeadBytes + 64;
 }
-
-// shared memory per ring stage besides the stage itself: its flush slot
-size_t red_bytes(int mt) { return (size_t)gemv::kConsumerWarps * gemv::kTileRows * mt * 4; }
 
 size_t smem_cap() { return (size_t)std::min(max_smem_optin(), 227 * 1024 / gemv::kCtasPerSm - (gemv::kCtasPerSm - 1) * 1024); }
 
 int stages_for(const ts_qweight& w, const Plan& p, int mt) {
   const size_t f = fixed_smem(w, p, mt);
   if (f >= smem_cap()) return 0;
-  return (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - f) / (p.stage_bytes + red_bytes(mt)));
+  return (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - f) / p.stage_bytes);
 }
 
 template <int BITS, bool CB, bool DQ, int SEG, int NL>
@@ -1502,7 +1456,7 @@ int run_gemv(const GemvOp& op, int64_t M, void* workspace, size_t ws_bytes, cuda
     a.m0 = m0;
     a.mt = (int)std::min<int64_t>(max_mt, M - m0);
     a.stages = stages_for(w, p, a.mt);
-    const size_t smem = fixed_smem(w, p, a.mt) + (size_t)a.stages * (p.stage_bytes + red_bytes(a.mt));
+    const size_t smem = fixed_smem(w, p, a.mt) + (size_t)a.stages * p.stage_bytes;
     rc = launch_chain<1>(w, p.seg_chunks, c, p.grid, stream, smem);
     if (rc != TS_OK) return rc;
   }
@@ -1552,14 +1506,14 @@ int run_gemv_chain(const GemvOp* ops, int n, int64_t M, void* workspace, size_t 
     stage_bytes = std::max(stage_bytes, p.stage_bytes);   // rows first, then the layer's metadata
   }
   TS_UNSUPPORTED(fixed < smem_cap(), "qlinear chain: shared memory");
-  stages = (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - fixed) / (stage_bytes + red_bytes((int)M)));
+  stages = (int)std::min<size_t>(gemv::kMaxStages, (smem_cap() - fixed) / stage_bytes);
   TS_UNSUPPORTED(stages >= 2, "qlinear chain: shared memory for two stages");
   c.L[0].stall = take_test_stall() ? 1 : 0;
   for (int i = 0; i < n; ++i) {
     c.L[i].stages = stages;
     c.L[i].stage_bytes = stage_bytes;
   }
-  const size_t smem = fixed + (size_t)stages * (stage_bytes + red_bytes((int)M));
+  const size_t smem = fixed + (size_t)stages * stage_bytes;
   return launch_chain<gemv::kMaxChain>(*ops[0].w, seg, c, grid, stream, smem);
 }
 

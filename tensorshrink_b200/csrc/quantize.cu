@@ -163,17 +163,27 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float
     const int64_t it = base + threadIdx.x;
     float mn = INFINITY, mx = -INFINITY;
     int64_t r = 0, c0 = 0;
+    float v[8];
+    uint32_t k[8];
     if (it < items) {
       r = row_of(g, it);
       c0 = (it - r * g.n8) * 8;
-      float v[8];
-      uint32_t k[8];
       load8<DT>(g, r, c0, v, k);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         mn = fminf(mn, v[j]);
         mx = fmaxf(mx, v[j]);
-        if (do_hist && c0 + j < g.cols) atomicAdd(&hw[k[j] >> (E::KEY_BITS - E::L1_BITS)], 1u);
+      }
+    }
+    if (do_hist) {
+      // magnitudes crowd into a few bins: lanes with the same bin add once
+      // (one shared-memory atomic per distinct bin of the warp, not per lane)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool valid = it < items && c0 + j < g.cols;
+        const uint32_t bin = valid ? k[j] >> (E::KEY_BITS - E::L1_BITS) : 0xFFFFFFFFu;
+        const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+        if (valid && (threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&hw[bin], (uint32_t)__popc(peers));
       }
     }
     mn = group_reduce_min(mn, gw);
@@ -268,28 +278,42 @@ __global__ void __launch_bounds__(kThreads) cta_hist_kernel(const Geometry g, co
   uint32_t above = 0;
   if (g.vec) {
     // 8 keys per 16/32-byte vector (the range starts on a row, rows are whole vectors)
+    // two vectors per thread per iteration, both loads issued first
     const int64_t e_end = r1 * g.cols;
-    for (int64_t e = r0 * g.cols + 8 * (int64_t)threadIdx.x; e < e_end; e += 8 * kThreads) {
-      uint32_t k[8];
-      if (DT == TS_F32) {
-        const uint4 u0 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e);
-        const uint4 u1 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e + 4);
-        const uint32_t b[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    for (int64_t e0 = r0 * g.cols + 8 * (int64_t)threadIdx.x; e0 < e_end; e0 += 16 * kThreads) {
+      uint32_t k[2][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) k[j] = b[j] & 0x7FFFFFFFu;
-      } else {
-        const uint4 u = ldg_stream_v4(reinterpret_cast<const uint16_t*>(g.w) + e);
-        const uint32_t b[4] = {u.x, u.y, u.z, u.w};
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int64_t e = e0 + h2 * 8 * kThreads;
+        if (e >= e_end) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) k[j] = (b[j >> 1] >> (16 * (j & 1))) & 0x7FFFu;
+          for (int j = 0; j < 8; ++j) k[h2][j] = 0u;
+          continue;
+        }
+        if (DT == TS_F32) {
+          const uint4 u0 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e);
+          const uint4 u1 = ldg_stream_v4(reinterpret_cast<const float*>(g.w) + e + 4);
+          const uint32_t b[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) k[h2][j] = b[j] & 0x7FFFFFFFu;
+        } else {
+          const uint4 u = ldg_stream_v4(reinterpret_cast<const uint16_t*>(g.w) + e);
+          const uint32_t b[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) k[h2][j] = (b[j >> 1] >> (16 * (j & 1))) & 0x7FFFu;
+        }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t hi = k[j] >> E::LAST_BITS;
-        if (hi > prefix)
-          ++above;
-        else if (hi == prefix)
-          atomicAdd(&h[k[j] & (NB - 1)], 1u);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        if (e0 + h2 * 8 * kThreads >= e_end) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t hi = k[h2][j] >> E::LAST_BITS;
+          if (hi > prefix)
+            ++above;
+          else if (hi == prefix)
+            atomicAdd(&h[k[h2][j] & (NB - 1)], 1u);
+        }
       }
     }
   } else {
@@ -471,17 +495,33 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
   const int64_t r0 = blockIdx.x * a.plan.rows_per_cta;
   const int64_t r1 = min(g.rows, r0 + a.plan.rows_per_cta);
   const int64_t it0 = r0 * g.n8, it1 = r1 * g.n8;
+  // software pipeline: the next item's loads are issued before this item is
+  // processed, so two loads per thread are in flight
+  float vn[8];
+  uint32_t kn[8];
+  if (it0 + threadIdx.x < it1) {
+    const int64_t rr = row_of(g, it0 + threadIdx.x);
+    load8<DT>(g, rr, (it0 + threadIdx.x - rr * g.n8) * 8, vn, kn);
+  }
   for (int64_t base = it0; base < it1; base += kThreads) {
     const int64_t it = base + threadIdx.x;
     const bool live = it < it1;
     int64_t r = 0, c0 = 0;
     float v[8];
     uint32_t keys[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = vn[j];
+      keys[j] = kn[j];
+    }
+    if (it + kThreads < it1) {
+      const int64_t rn = row_of(g, it + kThreads);
+      load8<DT>(g, rn, (it + kThreads - rn * g.n8) * 8, vn, kn);
+    }
     int sel_gt = 0, n_eq = 0;
     if (live) {
       r = row_of(g, it);
       c0 = (it - r * g.n8) * 8;
-      load8<DT>(g, r, c0, v, keys);
       if (has_t) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -903,7 +943,8 @@ inline int last_bins(int dtype) { return dtype == TS_F32 ? 1024 : 128; }
 
 inline CtaPlan make_plan(int64_t rows) {
   CtaPlan p;
-  const int64_t target = qz::i64max(1, (int64_t)sm_count() * 4);
+  // about six 256-thread CTAs per SM (the select step takes at most 1024)
+  const int64_t target = qz::i64max(1, qz::i64min(1024, (int64_t)sm_count() * 6));
   p.rows_per_cta = qz::i64max(1, (rows + target - 1) / target);
   p.n_cta = (int)((rows + p.rows_per_cta - 1) / p.rows_per_cta);
   return p;

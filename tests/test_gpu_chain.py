@@ -70,6 +70,13 @@ def test_chain_equals_separate_launches(blocks, M, n_blocks):
     del before
     ref = _sequential(bl, x)
     torch.cuda.synchronize()
+    # one launch runs every layer in one build of the decode kernel, while
+    # single calls pick the build per layer (one or two CTAs per SM, whose
+    # warps split K differently): equal up to the fp32 summation order
+    got = outs[-1][1].float()
+    assert ((got - ref.float()).abs().max() / ref.float().abs().max()).item() < 1e-2
+    # one launch per layer: the same calls as the sequential reference
+    kernels.qlinear_chain(_chain_steps(bl, x, outs))
     assert torch.equal(outs[-1][1], ref)
     kernels.device_status()
 
@@ -87,8 +94,8 @@ def test_chain_repeats_and_replays_in_a_graph(blocks):
     for _ in range(3):
         kernels.qlinear_chain(steps, persistent=True)
         assert torch.equal(outs[-1][1], first)
-    kernels.qlinear_chain(steps)            # one launch per layer: the same result
-    assert torch.equal(outs[-1][1], first)
+    kernels.qlinear_chain(steps)            # one launch per layer
+    assert ((outs[-1][1].float() - first.float()).abs().max() / first.float().abs().max()).item() < 1e-2
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -190,4 +197,5 @@ def test_chain_wait_timeout_is_reported(blocks):
     kernels.qlinear_chain(steps, persistent=True)
     torch.cuda.synchronize()
     kernels.device_status()
-    assert torch.equal(outs[-1][1], _sequential(blocks[:2], x))
+    ref = _sequential(blocks[:2], x).float()
+    assert ((outs[-1][1].float() - ref).abs().max() / ref.abs().max()).item() < 1e-2
