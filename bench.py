@@ -1006,6 +1006,7 @@ def main():
     ap.add_argument("--only", choices=("decoder", "quantize", "prefill"), default=None,
                     help="run one study alone (short; for launch lists and profiles): the 8B decoder at "
                          "batch 1, the [28672, 8192] quantize, or the config-3 prefill layer")
+    ap.add_argument("--quant-shape", default="28672x8192", help="--only quantize: ROWSxCOLS of the weight")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed replays before the timed region (0 for profiling runs)")
     args = ap.parse_args()
@@ -1041,7 +1042,8 @@ def main():
             print(json.dumps(out), flush=True)
         return
     if args.only == "quantize":
-        print(json.dumps(quantize_measure(device, reps=max(1, args.steps))), flush=True)
+        rows, cols = (int(v) for v in args.quant_shape.split("x"))
+        print(json.dumps(quantize_measure(device, reps=max(1, args.steps), rows=rows, cols=cols)), flush=True)
         return
     if args.only == "prefill":
         print(json.dumps(prefill_measure(device, reps=max(1, args.steps))), flush=True)

@@ -53,6 +53,20 @@ constexpr int kPrefetchStages = 32;    // L2 prefetch distance of the code strea
 
 __device__ int g_err;           // wait-timeout flag, read and cleared by ts_qlinear_status
 
+#ifdef TS_QGEMM_PROF
+// Phase cycles of an instrumented build (never the shipped library), per CTA:
+// [0] MMA waits on loaded stages, [1] MMA waits on converted stages, [2] MMA
+// waits on the drained accumulator, [3] stages issued by the MMA thread,
+// [4] dequantizer (group 0, warp lane 0) waits on free TMEM stages, [5] its
+// waits on loaded stages, [6] its conversion cycles, [7] its store-wait
+// cycles, [8] its metadata waits, [9] producer waits on free stages,
+// [10] kernel cycles (MMA thread), [11] epilogue waits on the accumulator.
+__device__ unsigned long long g_qgemm_prof[512][12];
+#define TS_QPROF(...) __VA_ARGS__
+#else
+#define TS_QPROF(...)
+#endif
+
 struct Args {
   QW q;
   int64_t M;
@@ -318,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const QW& q = a.q;
 
   if (threadIdx.x == 0) {
+    TS_QPROF(for (int z = 0; z < 12; ++z) g_qgemm_prof[blockIdx.x][z] = 0;)
     for (int s = 0; s < S; ++s) {
       mbar_init(ld_full + s, 1);
       mbar_init(a_full + s, kDqGroupWarps);
@@ -384,7 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(slot + kBW * 16, &gmap, (kb / spm) * a.meta_groups, n0, m_full + ms);
             ++mit;
           }
+          TS_QPROF(long long q_p = clock64();)
           if (!mbar_wait_hint(empty + s, ph ^ 1, &g_err, 11, a.wait_ns)) { ok = false; break; }
+          TS_QPROF(g_qgemm_prof[blockIdx.x][9] += clock64() - q_p;)
           mbar_arrive_expect_tx(ld_full + s, kXStageBytes + kCStageBytes);
           tma_load_2d(sX + (size_t)s * kXStageBytes, &xmap, kb * kBK, m0, ld_full + s);
           tma_load_2d(sC + (size_t)s * kCStageBytes, &cmap, kb * kCodeBytes, n0, ld_full + s);
@@ -416,15 +433,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       int t_local = 0;
       ItemIter it = items_begin(a, ntiles);
       Item x;
+      TS_QPROF(unsigned long long* pr = g_qgemm_prof[blockIdx.x]; long long q_t0 = clock64();)
       while (ok && items_next(a, it, x)) {
+        TS_QPROF(long long q_a = clock64();)
         if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12, a.wait_ns)) { ok = false; break; }
+        TS_QPROF(pr[2] += clock64() - q_a;)
         tc_fence_after();
         for (int kb = x.k0; kb < x.k1; ++kb) {
-          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13, a.wait_ns) ||
-              !mbar_wait_hint(a_full + s, ph, &g_err, 13, a.wait_ns)) {
+          TS_QPROF(long long q_b = clock64();)
+          if (!mbar_wait_hint(ld_full + s, ph, &g_err, 13, a.wait_ns)) {
             ok = false;
             break;
           }
+          TS_QPROF(long long q_c = clock64(); pr[0] += q_c - q_b;)
+          if (!mbar_wait_hint(a_full + s, ph, &g_err, 13, a.wait_ns)) {
+            ok = false;
+            break;
+          }
+          TS_QPROF(pr[1] += clock64() - q_c; pr[3] += 1;)
           tc_fence_after();
           // stage s: B descriptor start advances by the stage size (16-byte units)
           const uint64_t bd = bd0 + (uint64_t)((s * kXStageBytes) >> 4);
@@ -438,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma_commit(tfull);
         ++t_local;
       }
+      TS_QPROF(pr[10] = clock64() - q_t0;)
       // every MMA issued (also those of an item abandoned after a timeout)
       // has finished before the TMEM is freed
       umma_commit(mma_drain);
@@ -636,10 +663,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nst = x.k1 - x.k0;
       for (int b = x.k0 / spm; ok && b * spm < x.k1; ++b) {
         const int kb_lo = max(x.k0, b * spm), kb_hi = min(x.k1, (b + 1) * spm);
+        TS_QPROF(long long q_m = clock64();)
         if (a.meta_tma && !mbar_wait_hint(m_full + (mit & 1), (mit >> 1) & 1, &g_err, 18, a.wait_ns)) {
           ok = false;
           break;
         }
+        TS_QPROF(if (warp == kFirstDqWarp && lane == 0) g_qgemm_prof[blockIdx.x][8] += clock64() - q_m;)
         const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
         // first stage of this group in the block: local index j = kb - k0 with j % 2 == grp
         int kb = kb_lo + (((kb_lo - x.k0) & 1) != grp ? 1 : 0);
@@ -668,8 +697,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           float2 sg[2];
           if (valid) decode(row_ng, kb, rawc, sg);
 
-          if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15, a.wait_ns) ||
-              !mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
+          TS_QPROF(const bool q_me = warp == kFirstDqWarp && lane == 0;
+                   unsigned long long* pq = g_qgemm_prof[blockIdx.x]; long long q_d = clock64();)
+          if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15, a.wait_ns)) { ok = false; break; }
+          TS_QPROF(long long q_e = clock64(); if (q_me) pq[4] += q_e - q_d;)
+          if (!mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
+          TS_QPROF(long long q_f = clock64(); if (q_me) pq[5] += q_f - q_e;)
           const unsigned char* crow = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes + half * (kCodeBytes / 2);
           uint32_t cw[kCodeBytes / 8];
           if (kCodeBytes / 2 >= 16) {
@@ -714,8 +747,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+          TS_QPROF(long long q_g = clock64(); if (q_me) pq[6] += q_g - q_f;)
           tmem_st16(lane_base + cs * kAStageCols, wv);
           tmem_st_wait();
+          TS_QPROF(if (q_me) pq[7] += clock64() - q_g;)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(a_full + cs);
@@ -971,5 +1006,15 @@ int qgemm_error_flag(int* code, bool clear, cudaStream_t stream) {
   return TS_OK;
 }
 
+#ifdef TS_QGEMM_PROF
+int qgemm_prof_read(void* dst) {
+  TS_CUDA_TRY(cudaMemcpyFromSymbol(dst, qgemm::g_qgemm_prof, sizeof(qgemm::g_qgemm_prof)));
+  return TS_OK;
+}
+#endif
 
 }  // namespace ts
+
+#ifdef TS_QGEMM_PROF
+extern "C" __attribute__((visibility("default"))) int ts_prof_read_qgemm(void* dst) { return ts::qgemm_prof_read(dst); }
+#endif

@@ -24,6 +24,7 @@
 // reference's order (subtract, then IEEE divide; round-half-even), so codes,
 // packed bytes, double-quant codes and deltas are bit-identical to it.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -84,6 +85,7 @@ struct Geometry {
   const void* w;
   int64_t rows, cols, padded_cols, n_groups, n8;  // n8 = padded_cols / 8 (items per row)
   int gs, bits;
+  int gs_shift;       // log2(gs) (group sizes are powers of two)
   uint64_t n8_magic;  // ceil(2^64 / n8) (0 when n8 == 1): row of item i = umul64hi(i, magic)
   int vec;            // rows are whole 16-byte vectors of 8 elements (cols % 8 == 0, aligned)
 };
@@ -173,23 +175,13 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float
       for (int j = 0; j < 8; ++j) {
         mn = fminf(mn, v[j]);
         mx = fmaxf(mx, v[j]);
-      }
-    }
-    if (do_hist) {
-      // magnitudes crowd into a few bins: lanes with the same bin add once
-      // (one shared-memory atomic per distinct bin of the warp, not per lane)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const bool valid = it < items && c0 + j < g.cols;
-        const uint32_t bin = valid ? k[j] >> (E::KEY_BITS - E::L1_BITS) : 0xFFFFFFFFu;
-        const uint32_t peers = __match_any_sync(0xffffffffu, bin);
-        if (valid && (threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&hw[bin], (uint32_t)__popc(peers));
+        if (do_hist && c0 + j < g.cols) atomicAdd(&hw[k[j] >> (E::KEY_BITS - E::L1_BITS)], 1u);
       }
     }
     mn = group_reduce_min(mn, gw);
     mx = group_reduce_max(mx, gw);
-    if (it < items && (threadIdx.x % gw) == 0) {
-      const int64_t grp = c0 / g.gs;
+    if (it < items && (threadIdx.x & (gw - 1)) == 0) {
+      const int64_t grp = c0 >> g.gs_shift;
       gmin_raw[r * g.n_groups + grp] = mn;
       gmax_raw[r * g.n_groups + grp] = mx;
     }
@@ -442,6 +434,7 @@ struct QuantArgs {
   int32_t* out_idx;
   uint16_t* out_val;
   int w_dtype;
+  int prefetch;             // issue the next item's loads before processing this one
 };
 
 template <int DT>
@@ -495,11 +488,11 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
   const int64_t r0 = blockIdx.x * a.plan.rows_per_cta;
   const int64_t r1 = min(g.rows, r0 + a.plan.rows_per_cta);
   const int64_t it0 = r0 * g.n8, it1 = r1 * g.n8;
-  // software pipeline: the next item's loads are issued before this item is
-  // processed, so two loads per thread are in flight
+  // software pipeline (a.prefetch): the next item's loads are issued before
+  // this item is processed, so two loads per thread are in flight
   float vn[8];
   uint32_t kn[8];
-  if (it0 + threadIdx.x < it1) {
+  if (a.prefetch && it0 + threadIdx.x < it1) {
     const int64_t rr = row_of(g, it0 + threadIdx.x);
     load8<DT>(g, rr, (it0 + threadIdx.x - rr * g.n8) * 8, vn, kn);
   }
@@ -509,14 +502,19 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
     int64_t r = 0, c0 = 0;
     float v[8];
     uint32_t keys[8];
+    if (a.prefetch) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      v[j] = vn[j];
-      keys[j] = kn[j];
-    }
-    if (it + kThreads < it1) {
-      const int64_t rn = row_of(g, it + kThreads);
-      load8<DT>(g, rn, (it + kThreads - rn * g.n8) * 8, vn, kn);
+      for (int j = 0; j < 8; ++j) {
+        v[j] = vn[j];
+        keys[j] = kn[j];
+      }
+      if (it + kThreads < it1) {
+        const int64_t rn = row_of(g, it + kThreads);
+        load8<DT>(g, rn, (it + kThreads - rn * g.n8) * 8, vn, kn);
+      }
+    } else if (live) {
+      const int64_t rl = row_of(g, it);
+      load8<DT>(g, rl, (it - rl * g.n8) * 8, v, keys);
     }
     int sel_gt = 0, n_eq = 0;
     if (live) {
@@ -534,7 +532,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
     }
     // ---- codes ----
     if (live) {
-      const int64_t grp = c0 / g.gs;
+      const int64_t grp = c0 >> g.gs_shift;
       const int64_t gi = r * g.n_groups + grp;
       // clamp(min) / clamp(max) of the raw range == range of the clamped group
       const float gmn = fminf(fmaxf(a.gmin_raw[gi], -tval), tval);
@@ -597,7 +595,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
         }
         *reinterpret_cast<uint2*>(prow + c0) = wv;
       }
-      if (c0 % g.gs == 0) {
+      if ((c0 & (g.gs - 1)) == 0) {
         a.scale[gi] = f2h(scale);                              // codec.py:637-638
         a.gmin[gi] = f2h(gmn);
       }
@@ -918,7 +916,7 @@ __global__ void lloyd_gather_kernel(const Geometry g, const SelState* st, const 
        j += (int64_t)gridDim.x * blockDim.x) {
     const int64_t f = sample ? sample[j] : j;
     const int64_t r = f / g.padded_cols, c = f - r * g.padded_cols;
-    const int64_t gi = r * g.n_groups + c / g.gs;
+    const int64_t gi = r * g.n_groups + (c >> g.gs_shift);
     const float gmn = fminf(fmaxf(gmin_raw[gi], -tval), tval);
     const float gmx = fminf(fmaxf(gmax_raw[gi], -tval), tval);
     const float scale = fmaxf(__fdiv_rn(__fsub_rn(gmx, gmn), levels), 1e-8f);
@@ -943,8 +941,14 @@ inline int last_bins(int dtype) { return dtype == TS_F32 ? 1024 : 128; }
 
 inline CtaPlan make_plan(int64_t rows) {
   CtaPlan p;
-  // about six 256-thread CTAs per SM (the select step takes at most 1024)
-  const int64_t target = qz::i64max(1, qz::i64min(1024, (int64_t)sm_count() * 6));
+  // 256-thread CTAs per SM for passes B and C (the select step takes at most
+  // 1024 CTAs); TS_QZ_CTAS_PER_SM overrides the default of 4 (tuning knob)
+  static const int per_sm = [] {
+    const char* k = getenv("TS_QZ_CTAS_PER_SM");
+    const int v = k ? atoi(k) : 0;
+    return v >= 1 && v <= 8 ? v : 4;
+  }();
+  const int64_t target = qz::i64max(1, qz::i64min(1024, (int64_t)sm_count() * per_sm));
   p.rows_per_cta = qz::i64max(1, (rows + target - 1) / target);
   p.n_cta = (int)((rows + p.rows_per_cta - 1) / p.rows_per_cta);
   return p;
@@ -991,6 +995,8 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
   g.rows = p.rows;
   g.cols = p.cols;
   g.gs = p.group_size;
+  g.gs_shift = 0;
+  while ((1 << g.gs_shift) < p.group_size) ++g.gs_shift;
   g.bits = p.bits;
   g.padded_cols = (p.cols + p.group_size - 1) / p.group_size * p.group_size;
   g.n_groups = g.padded_cols / p.group_size;
@@ -1090,6 +1096,13 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
   qa.out_idx = o.outlier_idx;
   qa.out_val = o.outlier_val;
   qa.w_dtype = DT;
+  {
+    static const int prefetch = [] {   // TS_QZ_PREFETCH=1 turns the pass-C pipeline on (tuning knob)
+      const char* k = getenv("TS_QZ_PREFETCH");
+      return k && k[0] == '1' ? 1 : 0;
+    }();
+    qa.prefetch = prefetch;
+  }
   quantize_kernel<DT><<<plan.n_cta, kThreads, 0, stream>>>(qa);
   TS_LAUNCH_CHECK();
 
