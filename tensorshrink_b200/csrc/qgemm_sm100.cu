@@ -18,13 +18,14 @@
 //               (4 per stage) from TMEM (A) and shared memory (B)
 //   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one weight row per
 //               thread, 32 tokens per load), + bias, convert, coalesced stores
-//   warps 6-21  dequantizers, two groups taking alternate stages (a stage's
-//               conversion is one long dependent chain per thread, so two
-//               groups keep twice the work in flight): two threads per weight
-//               row, 32 columns each per stage, unpack codes to the activation
-//               dtype in registers, patch the row's outliers in place as
-//               fp32(base + delta) rounded once, and store the result into the
-//               stage's TMEM columns.
+//   warps 6-21  dequantizers, four groups of four warps taking every fourth
+//               stage (a stage's conversion is one long dependent chain per
+//               thread, so four groups keep four stages of work in flight):
+//               one thread per weight row (= its TMEM lane), 64 columns per
+//               stage, unpack codes to the activation dtype in registers,
+//               patch the row's outliers in place as fp32(base + delta)
+//               rounded once, and store the result into the stage's TMEM
+//               columns.
 //
 // Keeping the dequantized tile out of shared memory leaves shared-memory
 // bandwidth to the activation operand alone (the tensor core reads A from
@@ -42,8 +43,8 @@ namespace qgemm {
 constexpr int kBW = 128;        // weight rows per tile = UMMA M = TMEM lanes
 constexpr int kBK = 64;         // K per stage = one 128-byte swizzle row of 16-bit values
 constexpr int kEpiWarps = 4;
-constexpr int kDqGroups = 2;    // dequantizer groups, taking alternate stages
-constexpr int kDqGroupWarps = 8;  // per group: two per TMEM lane quadrant (one per half row)
+constexpr int kDqGroups = 4;    // dequantizer groups, taking every fourth stage
+constexpr int kDqGroupWarps = 4;  // per group: one per TMEM lane quadrant (one thread per stage row)
 constexpr int kDqWarps = kDqGroups * kDqGroupWarps;
 constexpr int kFirstDqWarp = 2 + kEpiWarps;
 constexpr int kThreads = (kFirstDqWarp + kDqWarps) * 32;
@@ -576,17 +577,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- dequantizers ----------------
-    const int quad = warp & 3;
-    const int half = ((warp - kFirstDqWarp) >> 2) & 1;   // columns [32 half, 32 half + 32) of a stage
-    const int grp = (warp - kFirstDqWarp) / kDqGroupWarps; // this group converts the item's stages j = grp, grp+2, ...
+    const int quad = warp & 3;                             // TMEM lane quadrant of this warp
+    const int grp = (warp - kFirstDqWarp) / kDqGroupWarps; // this group converts the item's stages j = grp (mod kDqGroups)
     const int rl = quad * 32 + lane;                      // tile row of this thread = TMEM lane
     const int gs = q.group_size;
     const bool dq = q.dqs_codes != nullptr;
-    const int gph = gs >= 32 ? 1 : 32 / gs;               // groups in this thread's 32 columns (1 or 2)
+    const int gph = gs >= 32 ? 1 : 32 / gs;               // groups in each 32-column half of the row (1 or 2)
     // Raw metadata of (row, group): 16-bit scale | 16-bit min << 16, or the
     // two double-quant code bytes, loaded by this thread (metadata rows that
     // are not 16-byte multiples).
-    auto fetch = [&](int64_t row, int kb, uint32_t (&raw)[2]) {
+    auto fetch = [&](int64_t row, int kb, int half, uint32_t (&raw)[2]) {
       if (row >= q.rows) return;
       const int64_t flat = row * q.n_groups + ((kb * kBK + 32 * half) >> a.gs_shift);
 #pragma unroll
@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    auto decode = [&](int64_t row_ng, int kb, const uint32_t (&raw)[2], float2 (&sg)[2]) {
+    auto decode = [&](int64_t row_ng, int kb, int half, const uint32_t (&raw)[2], float2 (&sg)[2]) {
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
         if (gi < gph) {
@@ -619,18 +619,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     // Ring position of the item's first stage (ts, tph) and the metadata
-    // block counter (both groups wait for and release every block of an item)
+    // block counter (every group waits for and releases every block of an item)
     uint32_t mit = 0, tph = 0;
     int ts = 0;
     bool ok = true;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + BT + half * (kAStageCols / 2);
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + BT;
     ItemIter it = items_begin(a, ntiles);
     Item x;
     while (ok && items_next(a, it, x)) {
       const int64_t row = (int64_t)(x.tile / a.tblocks) * kBW + rl;
       const bool valid = row < q.rows;
       const int64_t row_ng = row * q.n_groups;
-      const int my_par = (x.k0 + grp) & 1;                // parity of the stages this group converts
+      const int my_mod = (x.k0 + grp) % kDqGroups;        // stage index (mod kDqGroups) this group converts
       // Outliers of this row inside the item's columns. Column-sorted rows use
       // a cursor whose next (column, delta) is loaded right after the previous
       // patch; other rows scan their table.
@@ -650,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         next_col = INT_MAX;
         while (cur < o_end) {
           const int c = q.ocol[cur];
-          if (c >= col_lo && c < col_hi && ((c >> 5) & 1) == half && ((c >> 6) & 1) == my_par) {
+          if (c >= col_lo && c < col_hi && ((c >> 6) % kDqGroups) == my_mod) {
             next_col = c;
             next_delta = __half2float(q.odelta[cur]);
             break;
@@ -670,32 +670,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         TS_QPROF(if (warp == kFirstDqWarp && lane == 0) g_qgemm_prof[blockIdx.x][8] += clock64() - q_m;)
         const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
-        // first stage of this group in the block: local index j = kb - k0 with j % 2 == grp
-        int kb = kb_lo + (((kb_lo - x.k0) & 1) != grp ? 1 : 0);
+        // first stage of this group in the block: local index j = kb - k0 with j % kDqGroups == grp
+        int kb = kb_lo + ((grp - (kb_lo - x.k0)) % kDqGroups + kDqGroups) % kDqGroups;
         for (; kb < kb_hi; kb += kDqGroups) {
           const int j = kb - x.k0;
           const int sp = ts + j;
           const int cs = sp % S;
           const uint32_t cph = tph ^ (uint32_t)((sp / S) & 1);
-          const int c0 = kb * kBK + 32 * half;                // first column of this thread's half
-          uint32_t rawc[2] = {0, 0};
-          if (a.meta_tma) {
-            const int ib = (((kb % spm) << 6) + 32 * half) >> a.gs_shift;   // group of c0 within the block
+          uint32_t rawc2[2][2] = {{0, 0}, {0, 0}};   // metadata of each half, decoded when it is converted
 #pragma unroll
-            for (int gi = 0; gi < 2; ++gi) {
-              if (gi < gph) {
-                if (dq)
-                  rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[kBW * 16 + ib + gi] << 8);
-                else
-                  rawc[gi] = (uint32_t)reinterpret_cast<const uint16_t*>(slot)[ib + gi] |
-                             ((uint32_t)reinterpret_cast<const uint16_t*>(slot + kBW * 16)[ib + gi] << 16);
+          for (int half = 0; half < 2; ++half) {
+            uint32_t (&rawc)[2] = rawc2[half];
+            if (a.meta_tma) {
+              const int ib = (((kb % spm) << 6) + 32 * half) >> a.gs_shift;   // group of the half within the block
+#pragma unroll
+              for (int gi = 0; gi < 2; ++gi) {
+                if (gi < gph) {
+                  if (dq)
+                    rawc[gi] = (uint32_t)slot[ib + gi] | ((uint32_t)slot[kBW * 16 + ib + gi] << 8);
+                  else
+                    rawc[gi] = (uint32_t)reinterpret_cast<const uint16_t*>(slot)[ib + gi] |
+                               ((uint32_t)reinterpret_cast<const uint16_t*>(slot + kBW * 16)[ib + gi] << 16);
+                }
               }
+            } else {
+              fetch(row, kb, half, rawc);
             }
-          } else {
-            fetch(row, kb, rawc);
           }
-          float2 sg[2];
-          if (valid) decode(row_ng, kb, rawc, sg);
 
           TS_QPROF(const bool q_me = warp == kFirstDqWarp && lane == 0;
                    unsigned long long* pq = g_qgemm_prof[blockIdx.x]; long long q_d = clock64();)
@@ -703,52 +704,60 @@ __global__ void __launch_bounds__(kThreads, 1)
           TS_QPROF(long long q_e = clock64(); if (q_me) pq[4] += q_e - q_d;)
           if (!mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
           TS_QPROF(long long q_f = clock64(); if (q_me) pq[5] += q_f - q_e;)
-          const unsigned char* crow = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes + half * (kCodeBytes / 2);
-          uint32_t cw[kCodeBytes / 8];
-          if (kCodeBytes / 2 >= 16) {
+          const unsigned char* crow_all = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes;
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            const int c0 = kb * kBK + 32 * half;                // first column of this half
+            const unsigned char* crow = crow_all + half * (kCodeBytes / 2);
+            uint32_t cw[kCodeBytes / 8];
+            if (kCodeBytes / 2 >= 16) {
 #pragma unroll
-            for (int i2 = 0; i2 < kCodeBytes / 32; ++i2) {
-              const uint4 u = reinterpret_cast<const uint4*>(crow)[i2];
-              cw[4 * i2] = u.x; cw[4 * i2 + 1] = u.y; cw[4 * i2 + 2] = u.z; cw[4 * i2 + 3] = u.w;
-            }
-          } else {
-            const uint2 u = *reinterpret_cast<const uint2*>(crow);
-            cw[0] = u.x; cw[kCodeBytes / 8 - 1] = u.y;
-          }
-          uint32_t wv[16];
-          if (!valid) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) wv[jj] = 0;
-          } else if (gph == 1) {
-            convert_half<BITS, CB, XT, 1>(cw, sg, cbs, wv);
-          } else {
-            convert_half<BITS, CB, XT, 2>(cw, sg, cbs, wv);
-          }
-          // outliers in this thread's 32 columns: value = fp32(base) + delta, rounded once
-          if (valid && o_end > o_beg) {
-            if (sorted) {
-              while (next_col < c0 + 32) {
-                const int cc = next_col - c0;
-                const uint32_t byte = crow[cc * BITS / 8];
-                const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
-                const float2 g = (gph == 2 && cc >= 16) ? sg[1] : sg[0];
-                const float v = CB ? cbs[code] : (float)code;
-                const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
-                patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
-                ++cur;
-                advance();
+              for (int i2 = 0; i2 < kCodeBytes / 32; ++i2) {
+                const uint4 u = reinterpret_cast<const uint4*>(crow)[i2];
+                cw[4 * i2] = u.x; cw[4 * i2 + 1] = u.y; cw[4 * i2 + 2] = u.z; cw[4 * i2 + 3] = u.w;
               }
             } else {
-              for (int jo = o_beg; jo < o_end; ++jo) {
-                const int c = q.ocol[jo];
-                if (c < c0 || c >= c0 + 32) continue;
-                const float val = outlier_value<CB>(q, cbs, row, c, jo);
-                patch_half(wv, c - c0, pack2<XT>(val, val) & 0xFFFFu);
+              const uint2 u = *reinterpret_cast<const uint2*>(crow);
+              cw[0] = u.x; cw[kCodeBytes / 8 - 1] = u.y;
+            }
+            float2 sgh[2];
+            const uint32_t rh[2] = {half ? rawc2[1][0] : rawc2[0][0], half ? rawc2[1][1] : rawc2[0][1]};
+            if (valid) decode(row_ng, kb, half, rh, sgh);
+            uint32_t wv[16];
+            if (!valid) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) wv[jj] = 0;
+            } else if (gph == 1) {
+              convert_half<BITS, CB, XT, 1>(cw, sgh, cbs, wv);
+            } else {
+              convert_half<BITS, CB, XT, 2>(cw, sgh, cbs, wv);
+            }
+            // outliers in these 32 columns: value = fp32(base) + delta, rounded once
+            if (valid && o_end > o_beg) {
+              if (sorted) {
+                while (next_col < c0 + 32) {
+                  const int cc = next_col - c0;
+                  const uint32_t byte = crow[cc * BITS / 8];
+                  const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
+                  const float2 g = (gph == 2 && cc >= 16) ? sgh[1] : sgh[0];
+                  const float v = CB ? cbs[code] : (float)code;
+                  const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
+                  patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
+                  ++cur;
+                  advance();
+                }
+              } else {
+                for (int jo = o_beg; jo < o_end; ++jo) {
+                  const int c = q.ocol[jo];
+                  if (c < c0 || c >= c0 + 32) continue;
+                  const float val = outlier_value<CB>(q, cbs, row, c, jo);
+                  patch_half(wv, c - c0, pack2<XT>(val, val) & 0xFFFFu);
+                }
               }
             }
+            tmem_st16(lane_base + cs * kAStageCols + half * (kAStageCols / 2), wv);
           }
           TS_QPROF(long long q_g = clock64(); if (q_me) pq[6] += q_g - q_f;)
-          tmem_st16(lane_base + cs * kAStageCols, wv);
           tmem_st_wait();
           TS_QPROF(if (q_me) pq[7] += clock64() - q_g;)
           tc_fence_before();
