@@ -375,6 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       bool ok = true;
       uint32_t issued = 0;   // stages issued (ring position = issued % S)
+      TS_QPROF(long long q_pw = 0;)
       ItemIter it = items_begin(a, ntiles);
       Item x;
       while (ok && items_next(a, it, x)) {
@@ -402,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           TS_QPROF(long long q_p = clock64();)
           if (!mbar_wait_hint(empty + s, ph ^ 1, &g_err, 11, a.wait_ns)) { ok = false; break; }
-          TS_QPROF(g_qgemm_prof[blockIdx.x][9] += clock64() - q_p;)
+          TS_QPROF(q_pw += clock64() - q_p;)
           mbar_arrive_expect_tx(ld_full + s, kXStageBytes + kCStageBytes);
           tma_load_2d(sX + (size_t)s * kXStageBytes, &xmap, kb * kBK, m0, ld_full + s);
           tma_load_2d(sC + (size_t)s * kCStageBytes, &cmap, kb * kCodeBytes, n0, ld_full + s);
@@ -418,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t k = mit > 2 ? mit - 2 : 0; k < mit; ++k)
           mbar_wait_hint(m_full + (k & 1), (k >> 1) & 1, nullptr, 0, a.wait_ns);
       }
+      TS_QPROF(g_qgemm_prof[blockIdx.x][9] = q_pw;)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int t_local = 0;
       ItemIter it = items_begin(a, ntiles);
       Item x;
-      TS_QPROF(unsigned long long* pr = g_qgemm_prof[blockIdx.x]; long long q_t0 = clock64();)
+      TS_QPROF(long long q_t0 = clock64(); long long pr[4] = {0, 0, 0, 0};)
       while (ok && items_next(a, it, x)) {
         TS_QPROF(long long q_a = clock64();)
         if (!mbar_wait_hint(tempty, (t_local & 1) ^ 1, &g_err, 12, a.wait_ns)) { ok = false; break; }
@@ -465,7 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma_commit(tfull);
         ++t_local;
       }
-      TS_QPROF(pr[10] = clock64() - q_t0;)
+      TS_QPROF(unsigned long long* pg = g_qgemm_prof[blockIdx.x]; pg[10] = clock64() - q_t0;
+               for (int z = 0; z < 4; ++z) pg[z] = pr[z];)
       // every MMA issued (also those of an item abandoned after a timeout)
       // has finished before the TMEM is freed
       umma_commit(mma_drain);
@@ -624,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int ts = 0;
     bool ok = true;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + BT;
+    TS_QPROF(long long dqa[5] = {0, 0, 0, 0, 0};)   // waits free / loaded, convert, store wait, metadata
     ItemIter it = items_begin(a, ntiles);
     Item x;
     while (ok && items_next(a, it, x)) {
@@ -668,21 +672,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        TS_QPROF(if (warp == kFirstDqWarp && lane == 0) g_qgemm_prof[blockIdx.x][8] += clock64() - q_m;)
+        TS_QPROF(dqa[4] += clock64() - q_m;)
         const unsigned char* slot = sM + (size_t)(mit & 1) * kMSlotBytes + rl * 16;
         // first stage of this group in the block: local index j = kb - k0 with j % kDqGroups == grp
         int kb = kb_lo + ((grp - (kb_lo - x.k0)) % kDqGroups + kDqGroups) % kDqGroups;
+        // ring slot and phase of stage kb (one division per block; the loop
+        // below advances them by kDqGroups stages at a time)
+        int cs = ts + (kb - x.k0);
+        uint32_t cph = tph;
+        {
+          const int wr = cs / S;
+          cs -= wr * S;
+          cph ^= (uint32_t)(wr & 1);
+        }
+        int kb_in_block = kb - b * spm;
         for (; kb < kb_hi; kb += kDqGroups) {
-          const int j = kb - x.k0;
-          const int sp = ts + j;
-          const int cs = sp % S;
-          const uint32_t cph = tph ^ (uint32_t)((sp / S) & 1);
           uint32_t rawc2[2][2] = {{0, 0}, {0, 0}};   // metadata of each half, decoded when it is converted
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t (&rawc)[2] = rawc2[half];
             if (a.meta_tma) {
-              const int ib = (((kb % spm) << 6) + 32 * half) >> a.gs_shift;   // group of the half within the block
+              const int ib = ((kb_in_block << 6) + 32 * half) >> a.gs_shift;   // group of the half within the block
 #pragma unroll
               for (int gi = 0; gi < 2; ++gi) {
                 if (gi < gph) {
@@ -698,12 +708,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
 
-          TS_QPROF(const bool q_me = warp == kFirstDqWarp && lane == 0;
-                   unsigned long long* pq = g_qgemm_prof[blockIdx.x]; long long q_d = clock64();)
+          TS_QPROF(long long q_d = clock64();)
           if (!mbar_wait_hint(empty + cs, cph ^ 1, &g_err, 15, a.wait_ns)) { ok = false; break; }
-          TS_QPROF(long long q_e = clock64(); if (q_me) pq[4] += q_e - q_d;)
+          TS_QPROF(long long q_e = clock64(); dqa[0] += q_e - q_d;)
           if (!mbar_wait_hint(ld_full + cs, cph, &g_err, 16, a.wait_ns)) { ok = false; break; }
-          TS_QPROF(long long q_f = clock64(); if (q_me) pq[5] += q_f - q_e;)
+          TS_QPROF(long long q_f = clock64(); dqa[1] += q_f - q_e;)
           const unsigned char* crow_all = sC + (size_t)cs * kCStageBytes + rl * kCodeBytes;
 #pragma unroll 1
           for (int half = 0; half < 2; ++half) {
@@ -757,12 +766,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tmem_st16(lane_base + cs * kAStageCols + half * (kAStageCols / 2), wv);
           }
-          TS_QPROF(long long q_g = clock64(); if (q_me) pq[6] += q_g - q_f;)
+          TS_QPROF(long long q_g = clock64(); dqa[2] += q_g - q_f;)
           tmem_st_wait();
-          TS_QPROF(if (q_me) pq[7] += clock64() - q_g;)
+          TS_QPROF(dqa[3] += clock64() - q_g;)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(a_full + cs);
+          kb_in_block += kDqGroups;
+          cs += kDqGroups;
+          while (cs >= S) {
+            cs -= S;
+            cph ^= 1u;
+          }
         }
         if (!ok) break;
         if (a.meta_tma) {
@@ -779,6 +794,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ts = adv - wraps * S;
       tph ^= (uint32_t)(wraps & 1);
     }
+    TS_QPROF(if (warp == kFirstDqWarp && lane == 0) {
+      unsigned long long* pg = g_qgemm_prof[blockIdx.x];
+      for (int z = 0; z < 4; ++z) pg[4 + z] = dqa[z];
+      pg[8] = dqa[4];
+    })
   }
 
   tc_fence_before();
