@@ -16,8 +16,10 @@ measured device-side over a CUDA-graph replay of K steps; `e2e` runs the same
 steps through the public module API with the input copied from pinned host
 memory and the output copied back inside the timed region.
 
-Multi-GPU (torchrun, one process per GPU): each rank runs its own copy of the
-workload ("scaling": "weak"); time is the max over ranks.
+Multi-GPU (torchrun, one process per GPU): the blocks are tensor-parallel
+(gate/up column-parallel, down row-parallel with its fp32 partial sums summed
+by the library's one-shot NVLink all-reduce kernel, or NCCL with --nccl), so
+the total work is fixed ("scaling": "strong"); time is the max over ranks.
 
 The same JSON line carries a `prefill` object: TFLOP/s of the BASELINE
 configs[2] layer ([8192, 8192], 2-bit Lloyd-Max g64, 0.1% outliers) at M=2048
