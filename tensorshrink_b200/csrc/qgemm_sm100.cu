@@ -88,6 +88,7 @@ struct Args {
   float* partials;   // split: [grid][2][128 rows][BT tokens] fp32
   int* counters;     // split: one per tile, zero between calls
   int prefetch_codes;  // L2-prefetch each item's code columns through cmap_wide
+  int qcap;          // outlier queue entries per dequantizer thread (0: read the tables in place)
 };
 
 // ---- dequantization of 8-column chunks ----------------------------------------
@@ -328,6 +329,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   float* cbs = reinterpret_cast<float*>(tmem_slot + 4);   // codebook copy (<= 256 floats)
   int* epi_flag = reinterpret_cast<int*>(cbs + 256);     // split: counter value seen by the epilogue
+  // per-dequantizer-thread outlier queues: [group][entry][128 rows] words of
+  // (column - item's first column) | fp16 delta << 16
+  uint32_t* oq = reinterpret_cast<uint32_t*>(epi_flag + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const QW& q = a.q;
@@ -635,18 +639,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = row < q.rows;
       const int64_t row_ng = row * q.n_groups;
       const int my_mod = (x.k0 + grp) % kDqGroups;        // stage index (mod kDqGroups) this group converts
-      // Outliers of this row inside the item's columns. Column-sorted rows use
-      // a cursor whose next (column, delta) is loaded right after the previous
-      // patch; other rows scan their table.
+      // Outliers of this row inside the item's columns. With a queue (qcap >
+      // 0) the entries of this group's stages are gathered at the item's
+      // start into this thread's shared-memory queue, sorted by column (the
+      // stage loop then reads them at shared-memory latency; the table's
+      // global loads are all independent and issued here, off the per-stage
+      // critical path). A row with more entries than the queue holds keeps
+      // the smallest columns and refills after the last one consumed.
+      // Without a queue, column-sorted rows use a cursor over the table and
+      // other rows scan it.
       int o_beg = 0, o_end = 0;
-      bool sorted = true;
       if (valid && q.n_outliers > 0) {
         o_beg = q.orow_ptr[row];
         o_end = q.orow_ptr[row + 1];
+      }
+      const int col_lo = x.k0 * kBK, col_hi = x.k1 * kBK;
+      const int QC = a.qcap;
+      uint32_t* oq_t = oq + (size_t)grp * QC * kBW + rl;   // entry e at oq_t[e * kBW]
+      int qn = 0, qi = 0;
+      bool qmore = false;
+      // gather the entries with column > after (relative to col_lo)
+      auto refill = [&](int after) {
+        qn = 0;
+        qi = 0;
+        qmore = false;
+        for (int j = o_beg; j < o_end; ++j) {
+          const int c = q.ocol[j];
+          const int cr = c - col_lo;
+          if (c < col_lo || c >= col_hi || cr <= after || ((c >> 6) % kDqGroups) != my_mod) continue;
+          if (qn == QC) {
+            qmore = true;
+            if ((int)(oq_t[(QC - 1) * kBW] & 0xFFFFu) < cr) continue;
+            --qn;   // drop the largest column; a later refill finds it again
+          }
+          const uint32_t e = (uint32_t)cr | ((uint32_t)__half_as_ushort(q.odelta[j]) << 16);
+          int p = qn;
+          while (p > 0 && (int)(oq_t[(p - 1) * kBW] & 0xFFFFu) > cr) {
+            oq_t[p * kBW] = oq_t[(p - 1) * kBW];
+            --p;
+          }
+          oq_t[p * kBW] = e;
+          ++qn;
+        }
+      };
+      int q_last = -1;   // relative column of the last entry consumed
+      bool sorted = true;
+      if (QC > 0) {
+        if (o_end > o_beg) refill(-1);
+      } else {
         for (int j = o_beg + 1; j < o_end; ++j)
           if (q.ocol[j] < q.ocol[j - 1]) { sorted = false; break; }
       }
-      const int col_lo = x.k0 * kBK, col_hi = x.k1 * kBK;
       int cur = o_beg;
       int next_col = INT_MAX;
       float next_delta = 0.f;
@@ -662,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++cur;
         }
       };
-      if (sorted) advance();
+      if (QC == 0 && sorted) advance();
 
       const int nst = x.k1 - x.k0;
       for (int b = x.k0 / spm; ok && b * spm < x.k1; ++b) {
@@ -743,7 +786,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // outliers in these 32 columns: value = fp32(base) + delta, rounded once
             if (valid && o_end > o_beg) {
-              if (sorted) {
+              if (QC > 0) {
+                while (true) {
+                  if (qi == qn) {
+                    if (!qmore) break;
+                    refill(q_last);
+                    if (qn == 0) break;
+                  }
+                  const uint32_t e = oq_t[qi * kBW];
+                  const int cc = (int)(e & 0xFFFFu) + col_lo - c0;
+                  if (cc >= 32) break;
+                  const uint32_t byte = crow[cc * BITS / 8];
+                  const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
+                  const float2 g = (gph == 2 && cc >= 16) ? sgh[1] : sgh[0];
+                  const float v = CB ? cbs[code] : (float)code;
+                  const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + __half2float(__ushort_as_half((unsigned short)(e >> 16)));
+                  patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
+                  q_last = (int)(e & 0xFFFFu);
+                  ++qi;
+                }
+              } else if (sorted) {
                 while (next_col < c0 + 32) {
                   const int cc = next_col - c0;
                   const uint32_t byte = crow[cc * BITS / 8];
@@ -813,9 +875,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---- host -------------------------------------------------------------------
 
-static size_t qgemm_smem(int BT, int bits, int S) {
+static size_t qgemm_smem(int BT, int bits, int S, int qcap = 0) {
   const size_t stage = (size_t)BT * qgemm::kBK * 2 + (size_t)qgemm::kBW * qgemm::kBK * bits / 8;
-  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 9) * 8 + 16 + 256 * 4 + 16;
+  return 1024 + (size_t)S * stage + 2 * (2 * (size_t)qgemm::kBW * 16) + (3 * S + 9) * 8 + 16 + 256 * 4 + 16 +
+         (size_t)qgemm::kDqGroups * qgemm::kBW * 4 * qcap;
+}
+
+// Outlier queue entries per dequantizer thread: up to kMaxQcap, in the shared
+// memory left after S stages (the caller may give up a stage for it).
+constexpr int kMaxQcap = 16;
+static int qgemm_qcap(int BT, int bits, int S) {
+  const size_t base = qgemm_smem(BT, bits, S, 0);
+  const size_t lim = (size_t)max_smem_optin();
+  if (base >= lim) return 0;
+  const size_t per = (size_t)qgemm::kDqGroups * qgemm::kBW * 4;
+  return (int)std::min<size_t>(kMaxQcap, (lim - base) / per);
 }
 
 static int max_stages(int BT) { return (qgemm::kTmemCols - BT) / qgemm::kAStageCols; }
@@ -961,8 +1035,16 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   const int BT = p.BT;
   int S = max_stages(BT);
   while (S > 2 && qgemm_smem(BT, w.bits, S) > (size_t)max_smem_optin()) --S;
+  // relative outlier columns are 16-bit; a queue of fewer than 4 entries
+  // would refill often, so a stage is given up for a longer one
+  int qcap = 0;
+  if (w.n_outliers > 0 && w.cols <= 65535) {
+    qcap = qgemm_qcap(BT, w.bits, S);
+    if (qcap < 4 && S > 3) qcap = qgemm_qcap(BT, w.bits, --S);
+  }
   a.stages = S;
-  const size_t smem = qgemm_smem(BT, w.bits, S);
+  a.qcap = qcap;
+  const size_t smem = qgemm_smem(BT, w.bits, S, qcap);
   const int grid = p.grid;
   CUtensorMap maps[5];
   int rc = encode_tmap_2d(&maps[0], x, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)w.cols, (uint64_t)M,

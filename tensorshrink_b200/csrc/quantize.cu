@@ -79,6 +79,8 @@ struct SelState {
   float t_val;          // |w| at the threshold
   int64_t n_gt;         // elements strictly above T
   int64_t need_eq;      // ties to keep
+  uint32_t floor_bin;   // pass A histograms only first-level bins >= this (a sampled lower bound of T)
+  int redo;             // the bound was too high: the bins below it are counted by the redo pass
 };
 
 struct Geometry {
@@ -143,21 +145,24 @@ __device__ __forceinline__ float group_reduce_max(float v, int width) {
 }
 
 // ---- pass A ------------------------------------------------------------------
+// Per-group min/max of the raw weight, and the first-level histogram of the
+// magnitude keys. Only bins >= st->floor_bin are counted: the threshold lies
+// at or above that bin whenever the counted elements number at least k
+// (checked by the first select, which otherwise has the redo pass count the
+// bins below). Few elements clear the bound, so few shared-memory atomics
+// are issued.
 template <int DT>
 __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float* gmin_raw,
                                                          float* gmax_raw, uint32_t* hist1,
-                                                         int do_hist) {
+                                                         int do_hist, const SelState* st) {
   using E = Elem<DT>;
   constexpr int NB = 1 << E::L1_BITS;
-  // one sub-histogram per warp for the 256-bin (16-bit) keys: magnitudes
-  // crowd into a few bins, and fewer threads per counter means fewer
-  // serialized shared-memory atomics
-  constexpr int NSUB = NB <= 256 ? kThreads / 32 : 1;
-  __shared__ uint32_t h[NSUB * NB];
+  constexpr int SH = E::KEY_BITS - E::L1_BITS;
+  __shared__ uint32_t h[NB];
   if (do_hist)
-    for (int i = threadIdx.x; i < NSUB * NB; i += kThreads) h[i] = 0;
+    for (int i = threadIdx.x; i < NB; i += kThreads) h[i] = 0;
   __syncthreads();
-  uint32_t* hw = h + (NSUB > 1 ? (threadIdx.x >> 5) * NB : 0);
+  const uint32_t floor_bin = do_hist ? st->floor_bin : 0u;
   const int gw = g.gs / 8;  // threads per group (power of two <= 32)
   const int64_t items = g.rows * g.n8;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
@@ -165,17 +170,46 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float
     const int64_t it = base + threadIdx.x;
     float mn = INFINITY, mx = -INFINITY;
     int64_t r = 0, c0 = 0;
-    float v[8];
-    uint32_t k[8];
     if (it < items) {
       r = row_of(g, it);
       c0 = (it - r * g.n8) * 8;
-      load8<DT>(g, r, c0, v, k);
+      if (DT != TS_F32 && g.vec && c0 + 8 <= g.cols) {
+        // 8 16-bit values: min/max on packed pairs (exact), keys from the raw bits
+        const uint4 u = ldg_stream_v4(reinterpret_cast<const uint16_t*>(g.w) + r * g.cols + c0);
+        const uint32_t b[4] = {u.x, u.y, u.z, u.w};
+        if (DT == TS_F16) {
+          __half2 lo = __hmin2(__hmin2(*reinterpret_cast<const __half2*>(&b[0]), *reinterpret_cast<const __half2*>(&b[1])),
+                               __hmin2(*reinterpret_cast<const __half2*>(&b[2]), *reinterpret_cast<const __half2*>(&b[3])));
+          __half2 hi = __hmax2(__hmax2(*reinterpret_cast<const __half2*>(&b[0]), *reinterpret_cast<const __half2*>(&b[1])),
+                               __hmax2(*reinterpret_cast<const __half2*>(&b[2]), *reinterpret_cast<const __half2*>(&b[3])));
+          mn = fminf(__low2float(lo), __high2float(lo));
+          mx = fmaxf(__low2float(hi), __high2float(hi));
+        } else {
+          using B2 = __nv_bfloat162;
+          B2 lo = __hmin2(__hmin2(*reinterpret_cast<const B2*>(&b[0]), *reinterpret_cast<const B2*>(&b[1])),
+                          __hmin2(*reinterpret_cast<const B2*>(&b[2]), *reinterpret_cast<const B2*>(&b[3])));
+          B2 hi = __hmax2(__hmax2(*reinterpret_cast<const B2*>(&b[0]), *reinterpret_cast<const B2*>(&b[1])),
+                          __hmax2(*reinterpret_cast<const B2*>(&b[2]), *reinterpret_cast<const B2*>(&b[3])));
+          mn = fminf(__low2float(lo), __high2float(lo));
+          mx = fmaxf(__low2float(hi), __high2float(hi));
+        }
+        if (do_hist) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        mn = fminf(mn, v[j]);
-        mx = fmaxf(mx, v[j]);
-        if (do_hist && c0 + j < g.cols) atomicAdd(&hw[k[j] >> (E::KEY_BITS - E::L1_BITS)], 1u);
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t bin = ((b[j >> 1] >> (16 * (j & 1))) & 0x7FFFu) >> SH;
+            if (bin >= floor_bin) atomicAdd(&h[bin], 1u);
+          }
+        }
+      } else {
+        float v[8];
+        uint32_t k[8];
+        load8<DT>(g, r, c0, v, k);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          mn = fminf(mn, v[j]);
+          mx = fmaxf(mx, v[j]);
+          if (do_hist && c0 + j < g.cols && (k[j] >> SH) >= floor_bin) atomicAdd(&h[k[j] >> SH], 1u);
+        }
       }
     }
     mn = group_reduce_min(mn, gw);
@@ -188,13 +222,71 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float
   }
   if (do_hist) {
     __syncthreads();
-    for (int i = threadIdx.x; i < NB; i += kThreads) {
-      uint32_t t = 0;
-#pragma unroll
-      for (int sub = 0; sub < NSUB; ++sub) t += h[sub * NB + i];
-      if (t) atomicAdd(hist1 + i, t);
-    }
+    for (int i = threadIdx.x; i < NB; i += kThreads)
+      if (h[i]) atomicAdd(hist1 + i, h[i]);
   }
+}
+
+// Lower bound of the threshold's first-level bin from a fixed, evenly spaced
+// sample of the keys (one block): the highest bin b such that the sampled
+// keys in bins >= b are at least 8x the expected share of the k largest plus
+// 64. Pass A then counts exactly the elements in bins >= b; if those number
+// fewer than k (the sample misled), the redo pass counts the rest, so the
+// selected threshold is exact either way.
+constexpr int kSampleThreads = 1024;
+constexpr int kSample = 65536;
+
+template <int DT>
+__global__ void __launch_bounds__(kSampleThreads) sample_bound_kernel(const Geometry g, int64_t k, SelState* st) {
+  using E = Elem<DT>;
+  constexpr int NB = 1 << E::L1_BITS;
+  constexpr int SH = E::KEY_BITS - E::L1_BITS;
+  __shared__ uint32_t h[NB];
+  for (int i = threadIdx.x; i < NB; i += kSampleThreads) h[i] = 0;
+  __syncthreads();
+  const int64_t n = g.rows * g.cols;
+  const int64_t S = n < kSample ? n : kSample;
+  for (int64_t si = threadIdx.x; si < S; si += kSampleThreads) {
+    const int64_t i = (int64_t)(((unsigned __int128)si * (unsigned __int128)n) / (unsigned __int128)S);
+    atomicAdd(&h[E::key(g.w, i) >> SH], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const double want = 8.0 * (double)k * (double)S / (double)n + 64.0;
+    uint32_t b = 0;
+    if (want < (double)S) {
+      uint64_t acc = 0;
+      for (int bb = NB - 1; bb >= 0; --bb) {
+        acc += h[bb];
+        if ((double)acc >= want) { b = (uint32_t)bb; break; }
+      }
+    }
+    st->floor_bin = b;
+    st->redo = 0;
+  }
+}
+
+// Redo pass: counts the first-level bins below the sampled bound when the
+// bins above it held fewer than k elements (never, in practice; every CTA
+// returns at once otherwise).
+template <int DT>
+__global__ void __launch_bounds__(kThreads) redo_hist_kernel(const Geometry g, uint32_t* hist1, const SelState* st) {
+  if (!st->redo) return;
+  using E = Elem<DT>;
+  constexpr int NB = 1 << E::L1_BITS;
+  constexpr int SH = E::KEY_BITS - E::L1_BITS;
+  __shared__ uint32_t h[NB];
+  for (int i = threadIdx.x; i < NB; i += kThreads) h[i] = 0;
+  __syncthreads();
+  const uint32_t floor_bin = st->floor_bin;
+  const int64_t n = g.rows * g.cols;
+  for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
+    const uint32_t bin = E::key(g.w, i) >> SH;
+    if (bin < floor_bin) atomicAdd(&h[bin], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NB; i += kThreads)
+    if (h[i]) atomicAdd(hist1 + i, h[i]);
 }
 
 // Find the bin holding rank k (1-based, counted from the largest) of a
@@ -222,6 +314,19 @@ __global__ void select_level_kernel(const uint32_t* hist, int nb, SelState* st, 
   int b;
   int64_t above;
   const int64_t kk = first ? k : st->k_rem;
+  if (first) {
+    // the first level's histogram counts only bins >= floor_bin: it must
+    // hold at least k elements, else the redo pass adds the bins below
+    int64_t tot = 0;
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) tot += hist[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if (tot < kk) {
+      if (threadIdx.x == 0) st->redo = 1;
+      return;
+    }
+    if (threadIdx.x == 0) st->redo = 0;
+  }
   select_bin(hist, nb, kk, &b, &above);
   if (threadIdx.x == 0) {
     st->prefix = first ? (uint32_t)b : ((st->prefix << level_bits) | (uint32_t)b);
@@ -485,6 +590,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
     tie_left = a.cta_info[2 * blockIdx.x + 1];
   }
   const float levels = (float)((1 << g.bits) - 1);
+  const int levels_i = (1 << g.bits) - 1;
   const int64_t r0 = blockIdx.x * a.plan.rows_per_cta;
   const int64_t r1 = min(g.rows, r0 + a.plan.rows_per_cta);
   const int64_t it0 = r0 * g.n8, it1 = r1 * g.n8;
@@ -521,11 +627,17 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
       r = row_of(g, it);
       c0 = (it - r * g.n8) * 8;
       if (has_t) {
+        // almost every item lies wholly below the threshold: one max first
+        uint32_t kmax = keys[0];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (c0 + j < g.cols) {
-            sel_gt += keys[j] > tkey;
-            n_eq += keys[j] == tkey;
+        for (int j = 1; j < 8; ++j) kmax = max(kmax, keys[j]);
+        if (kmax >= tkey) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (c0 + j < g.cols) {
+              sel_gt += keys[j] > tkey;
+              n_eq += keys[j] == tkey;
+            }
           }
         }
       }
@@ -571,8 +683,17 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const QuantArgs a) {
           }
           codes[j] = (uint32_t)lo;
         } else {
-          if (fabsf(t - floorf(t) - 0.5f) <= tol) t = __fdiv_rn(d, scale);
-          codes[j] = (uint32_t)fminf(fmaxf(rintf(t), 0.f), levels);
+          // t >= 0 (x >= the group minimum). Adding 1.5 * 2^23 rounds t to
+          // the nearest integer, ties to even, as rintf does, and leaves it
+          // in the low mantissa bits; t - rint(t) is exact, and t is within
+          // tol of a half-integer exactly when 0.5 - |t - rint(t)| <= tol.
+          constexpr float kMagic = 12582912.f;
+          float r = __fadd_rn(t, kMagic);
+          if (0.5f - fabsf(__fsub_rn(t, __fsub_rn(r, kMagic))) <= tol) {
+            t = __fdiv_rn(d, scale);
+            r = __fadd_rn(t, kMagic);
+          }
+          codes[j] = min(__float_as_uint(r) - 0x4B400000u, (uint32_t)levels_i);
         }
       }
       uint8_t* prow = a.packed + r * a.row_bytes;
@@ -1023,12 +1144,23 @@ int run_quantize(const void* w, const ts_quant_params& p, const ts_quant_outputs
   {
     const int64_t items = g.rows * g.n8;
     const int blocks = (int)qz::i64min((items + kThreads - 1) / kThreads, (int64_t)sms * 8);
-    stats_kernel<DT><<<std::max(blocks, 1), kThreads, 0, stream>>>(g, gmin_raw, gmax_raw, hist1, outliers);
+    if (outliers) {
+      sample_bound_kernel<DT><<<1, kSampleThreads, 0, stream>>>(g, p.k_outliers, st);
+      TS_LAUNCH_CHECK();
+    }
+    stats_kernel<DT><<<std::max(blocks, 1), kThreads, 0, stream>>>(g, gmin_raw, gmax_raw, hist1, outliers, st);
     TS_LAUNCH_CHECK();
   }
   if (outliers) {
     select_level_kernel<<<1, 32, 0, stream>>>(hist1, 1 << E::L1_BITS, st, 1, p.k_outliers, E::L1_BITS);
     TS_LAUNCH_CHECK();
+    {
+      const int blocks = (int)qz::i64min((n + kThreads - 1) / kThreads, (int64_t)sms * 8);
+      redo_hist_kernel<DT><<<blocks, kThreads, 0, stream>>>(g, hist1, st);
+      TS_LAUNCH_CHECK();
+      select_level_kernel<<<1, 32, 0, stream>>>(hist1, 1 << E::L1_BITS, st, 1, p.k_outliers, E::L1_BITS);
+      TS_LAUNCH_CHECK();
+    }
     if (E::L2_BITS) {
       const int blocks = (int)qz::i64min((n + kThreads - 1) / kThreads, (int64_t)sms * 8);
       prefix_hist_kernel<<<blocks, kThreads, 0, stream>>>(g, st, hist2);

@@ -138,3 +138,24 @@ def test_prefill_large_k_4bit():
     x = torch.randn(2048, 14336, device="cuda", dtype=torch.bfloat16)
     err = _rel(ql(x), _ref(x, W))
     assert err <= TOL, err
+
+
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_tensor_core_dense_outliers(shuffle):
+    """5% outliers (about 100 per row, far more than a dequantizer's outlier
+    queue holds, so it refills) in column order and in a shuffled order
+    within rows, on the prefill tiles and on the split decode plan."""
+    import numpy as np
+    import tensorshrink_b200 as ts
+    d = _layer(300, 2048, 4, 128, "uniform", False, seed=11, frac=0.05)
+    qt = d.to_quantized_tensor()
+    if shuffle:
+        perm = np.random.default_rng(0).permutation(qt.outlier_idx.shape[0])
+        qt.outlier_idx = qt.outlier_idx[perm]
+        qt.outlier_val = qt.outlier_val[perm]
+    ql = ts.QuantLinear(qt).cuda()
+    W = torch.from_numpy(goap.dequantize(qt)).cuda()
+    for M in (20, 64, 100, 300):
+        x = torch.randn(M, 2048, device="cuda", dtype=torch.bfloat16)
+        err = _rel(ql(x), _ref(x, W))
+        assert err <= TOL, (M, err)
