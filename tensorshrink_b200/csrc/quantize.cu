@@ -234,7 +234,8 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const Geometry g, float
 // fewer than k (the sample misled), the redo pass counts the rest, so the
 // selected threshold is exact either way.
 constexpr int kSampleThreads = 1024;
-constexpr int kSample = 65536;
+constexpr int kSamplePerThread = 4;
+constexpr int kSample = kSampleThreads * kSamplePerThread;
 
 template <int DT>
 __global__ void __launch_bounds__(kSampleThreads) sample_bound_kernel(const Geometry g, int64_t k, SelState* st) {
@@ -246,10 +247,16 @@ __global__ void __launch_bounds__(kSampleThreads) sample_bound_kernel(const Geom
   __syncthreads();
   const int64_t n = g.rows * g.cols;
   const int64_t S = n < kSample ? n : kSample;
-  for (int64_t si = threadIdx.x; si < S; si += kSampleThreads) {
-    const int64_t i = (int64_t)(((unsigned __int128)si * (unsigned __int128)n) / (unsigned __int128)S);
-    atomicAdd(&h[E::key(g.w, i) >> SH], 1u);
+  const int64_t step = n / S;   // sample si is element si * step
+  uint32_t kk[kSamplePerThread];
+#pragma unroll
+  for (int j = 0; j < kSamplePerThread; ++j) {   // all loads first, then the counts
+    const int64_t si = threadIdx.x + (int64_t)j * kSampleThreads;
+    kk[j] = si < S ? E::key(g.w, si * step) : 0xFFFFFFFFu;
   }
+#pragma unroll
+  for (int j = 0; j < kSamplePerThread; ++j)
+    if (kk[j] != 0xFFFFFFFFu) atomicAdd(&h[kk[j] >> SH], 1u);
   __syncthreads();
   if (threadIdx.x == 0) {
     const double want = 8.0 * (double)k * (double)S / (double)n + 64.0;
@@ -314,20 +321,44 @@ __global__ void select_level_kernel(const uint32_t* hist, int nb, SelState* st, 
   int b;
   int64_t above;
   const int64_t kk = first ? k : st->k_rem;
+  // one warp: lane t sums the t-th chunk of bins counted from the top, an
+  // inclusive scan finds the chunk where the count from the top reaches kk,
+  // and that lane walks its chunk
+  const int lane = threadIdx.x;
+  const int chunk = (nb + 31) / 32;
+  const int hi = nb - lane * chunk, lo = max(0, hi - chunk);
+  int64_t sum = 0;
+  for (int i = lo; i < hi; ++i) sum += hist[i];
+  int64_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const int64_t tot = __shfl_sync(0xffffffffu, incl, 31);
   if (first) {
     // the first level's histogram counts only bins >= floor_bin: it must
     // hold at least k elements, else the redo pass adds the bins below
-    int64_t tot = 0;
-    for (int i = threadIdx.x; i < nb; i += blockDim.x) tot += hist[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
     if (tot < kk) {
-      if (threadIdx.x == 0) st->redo = 1;
+      if (lane == 0) st->redo = 1;
       return;
     }
-    if (threadIdx.x == 0) st->redo = 0;
+    if (lane == 0) st->redo = 0;
   }
-  select_bin(hist, nb, kk, &b, &above);
+  const unsigned hit = __ballot_sync(0xffffffffu, incl >= kk);
+  const int owner = hit ? __ffs(hit) - 1 : 31;
+  b = 0;
+  above = tot;
+  if (lane == owner) {
+    int64_t acc = incl - sum;
+    for (int i = hi - 1; i >= lo; --i) {
+      if (acc + hist[i] >= kk) { b = i; break; }
+      acc += hist[i];
+    }
+    above = acc;
+  }
+  b = __shfl_sync(0xffffffffu, b, owner);
+  above = __shfl_sync(0xffffffffu, above, owner);
   if (threadIdx.x == 0) {
     st->prefix = first ? (uint32_t)b : ((st->prefix << level_bits) | (uint32_t)b);
     st->k_rem = kk - above;
