@@ -329,15 +329,20 @@ class QuantDecoder(nn.Module):
         decode_attention(b["qkv"], layer.n_heads_local, layer.n_kv_local, cfg.head_dim, pos, self.rope_cos,
                          self.rope_sin, self.k_cache[i], self.v_cache[i], attn_len, out=b["attn"])
         o, down = layer.o_proj.local, layer.down_proj.local
-        up_steps = [ChainStep(gu.qweight(), h, b["gu"], bias=gu.bias, norm_weight=layer.post_norm,
+
+        def up_steps(h_in):
+            # gate/up read the residual stream after the attention block's add
+            return [ChainStep(gu.qweight(), h_in, b["gu"], bias=gu.bias, norm_weight=layer.post_norm,
                               norm_eps=cfg.rms_eps, act_dtype=bf16)]
         if self.world == 1:
-            qlinear_chain([ChainStep(o.qweight(), b["attn"], h, bias=o.bias, residual=h)] + up_steps
+            # o_proj adds into h in place, so the chain's later steps see it
+            qlinear_chain([ChainStep(o.qweight(), b["attn"], h, bias=o.bias, residual=h)] + up_steps(h)
                           + [ChainStep(down.qweight(), b["gu"], h, bias=down.bias, gated=True, residual=h)])
             return h
         qlinear_chain([ChainStep(o.qweight(), b["attn"], b["part"], bias=o.bias if self.rank == 0 else None)])
+        # the reduction returns a new residual tensor: gate/up must read that one
         h = self._reduce_add(b["part"], h)
-        qlinear_chain(up_steps + [ChainStep(down.qweight(), b["gu"], b["part"],
+        qlinear_chain(up_steps(h) + [ChainStep(down.qweight(), b["gu"], b["part"],
                                             bias=down.bias if self.rank == 0 else None, gated=True)])
         return self._reduce_add(b["part"], h)
 
