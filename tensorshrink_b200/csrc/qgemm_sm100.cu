@@ -639,15 +639,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = row < q.rows;
       const int64_t row_ng = row * q.n_groups;
       const int my_mod = (x.k0 + grp) % kDqGroups;        // stage index (mod kDqGroups) this group converts
-      // Outliers of this row inside the item's columns. With a queue (qcap >
-      // 0) the entries of this group's stages are gathered at the item's
-      // start into this thread's shared-memory queue, sorted by column (the
-      // stage loop then reads them at shared-memory latency; the table's
-      // global loads are all independent and issued here, off the per-stage
-      // critical path). A row with more entries than the queue holds keeps
-      // the smallest columns and refills after the last one consumed.
-      // Without a queue, column-sorted rows use a cursor over the table and
-      // other rows scan it.
+      // Outliers of this row inside the item's columns: the entries of this
+      // group's stages are gathered at the item's start into this thread's
+      // shared-memory queue, sorted by column (so tables in any order within
+      // a row work), and the stage loop reads them at shared-memory latency.
+      // A row with more entries than the queue holds keeps the smallest
+      // columns and refills after the last one consumed. (The host always
+      // provides a queue when the weight has outliers.)
       int o_beg = 0, o_end = 0;
       if (valid && q.n_outliers > 0) {
         o_beg = q.orow_ptr[row];
@@ -683,29 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       int q_last = -1;   // relative column of the last entry consumed
-      bool sorted = true;
-      if (QC > 0) {
-        if (o_end > o_beg) refill(-1);
-      } else {
-        for (int j = o_beg + 1; j < o_end; ++j)
-          if (q.ocol[j] < q.ocol[j - 1]) { sorted = false; break; }
-      }
-      int cur = o_beg;
-      int next_col = INT_MAX;
-      float next_delta = 0.f;
-      auto advance = [&]() {
-        next_col = INT_MAX;
-        while (cur < o_end) {
-          const int c = q.ocol[cur];
-          if (c >= col_lo && c < col_hi && ((c >> 6) % kDqGroups) == my_mod) {
-            next_col = c;
-            next_delta = __half2float(q.odelta[cur]);
-            break;
-          }
-          ++cur;
-        }
-      };
-      if (QC == 0 && sorted) advance();
+      if (o_end > o_beg) refill(-1);
 
       const int nst = x.k1 - x.k0;
       for (int b = x.k0 / spm; ok && b * spm < x.k1; ++b) {
@@ -786,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // outliers in these 32 columns: value = fp32(base) + delta, rounded once
             if (valid && o_end > o_beg) {
-              if (QC > 0) {
+              {
                 while (true) {
                   if (qi == qn) {
                     if (!qmore) break;
@@ -804,25 +780,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                   patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
                   q_last = (int)(e & 0xFFFFu);
                   ++qi;
-                }
-              } else if (sorted) {
-                while (next_col < c0 + 32) {
-                  const int cc = next_col - c0;
-                  const uint32_t byte = crow[cc * BITS / 8];
-                  const int code = (int)((byte >> ((cc * BITS) & 7)) & ((1u << BITS) - 1));
-                  const float2 g = (gph == 2 && cc >= 16) ? sgh[1] : sgh[0];
-                  const float v = CB ? cbs[code] : (float)code;
-                  const float val = __fadd_rn(__fmul_rn(v, g.x), g.y) + next_delta;
-                  patch_half(wv, cc, pack2<XT>(val, val) & 0xFFFFu);
-                  ++cur;
-                  advance();
-                }
-              } else {
-                for (int jo = o_beg; jo < o_end; ++jo) {
-                  const int c = q.ocol[jo];
-                  if (c < c0 || c >= c0 + 32) continue;
-                  const float val = outlier_value<CB>(q, cbs, row, c, jo);
-                  patch_half(wv, c - c0, pack2<XT>(val, val) & 0xFFFFu);
                 }
               }
             }
@@ -904,6 +861,7 @@ static bool qgemm_layout_ok(const ts_qweight& w) {
   if (w.packed_row_bytes % 16 != 0 || !is_aligned(w.packed, 16)) return false;
   if (w.rows * w.n_groups >= (int64_t(1) << 31) || w.rows >= (int64_t(1) << 31)) return false;
   if (w.cols < 1) return false;
+  if (w.cols > 65535) return false;   // outlier queue entries hold 16-bit relative columns
   return max_smem_optin() >= (int)qgemm_smem(256, w.bits, 2);
 }
 
@@ -1038,9 +996,11 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   // relative outlier columns are 16-bit; a queue of fewer than 4 entries
   // would refill often, so a stage is given up for a longer one
   int qcap = 0;
-  if (w.n_outliers > 0 && w.cols <= 65535) {
+  if (w.n_outliers > 0) {
     qcap = qgemm_qcap(BT, w.bits, S);
     if (qcap < 4 && S > 3) qcap = qgemm_qcap(BT, w.bits, --S);
+    while (qcap < 1 && S > 2) qcap = qgemm_qcap(BT, w.bits, --S);
+    TS_UNSUPPORTED(qcap >= 1, "qgemm: no shared memory left for the outlier queues");
   }
   a.stages = S;
   a.qcap = qcap;
