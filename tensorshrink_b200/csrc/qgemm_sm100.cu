@@ -681,7 +681,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       int q_last = -1;   // relative column of the last entry consumed
-      if (o_end > o_beg) refill(-1);
+      // relative column of the next queue entry (INT_MAX: none left), kept
+      // in a register so a half without outliers costs one compare
+      int nx_c = INT_MAX;
+      if (o_end > o_beg) {
+        refill(-1);
+        if (qn > 0) nx_c = (int)(oq_t[0] & 0xFFFFu);
+      }
 
       const int nst = x.k1 - x.k0;
       for (int b = x.k0 / spm; ok && b * spm < x.k1; ++b) {
@@ -761,15 +767,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               convert_half<BITS, CB, XT, 2>(cw, sgh, cbs, wv);
             }
             // outliers in these 32 columns: value = fp32(base) + delta, rounded once
-            if (valid && o_end > o_beg) {
+            if (nx_c < c0 - col_lo + 32) {
               {
                 while (true) {
                   if (qi == qn) {
-                    if (!qmore) break;
+                    if (!qmore) { nx_c = INT_MAX; break; }
                     refill(q_last);
-                    if (qn == 0) break;
+                    if (qn == 0) { nx_c = INT_MAX; break; }
                   }
                   const uint32_t e = oq_t[qi * kBW];
+                  nx_c = (int)(e & 0xFFFFu);
                   const int cc = (int)(e & 0xFFFFu) + col_lo - c0;
                   if (cc >= 32) break;
                   const uint32_t byte = crow[cc * BITS / 8];
