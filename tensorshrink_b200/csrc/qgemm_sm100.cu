@@ -1004,7 +1004,13 @@ int run_qgemm(const ts_qweight& w, const void* x, int x_dtype, int64_t M, int64_
   // would refill often, so a stage is given up for a longer one
   int qcap = 0;
   if (w.n_outliers > 0) {
+    // queue length for a group's share of a row's outliers: mean + 2.5
+    // standard deviations (Poisson), so refills (a rescan of the row's table
+    // inside the stage loop) stay rare; a stage is given up to reach it
+    const double per_group = (double)w.n_outliers / (double)w.rows / qgemm::kDqGroups;
+    const int want = std::min(kMaxQcap, std::max(4, (int)std::ceil(per_group + 2.5 * std::sqrt(per_group))));
     qcap = qgemm_qcap(BT, w.bits, S);
+    if (qcap < want && S > 3 && qgemm_qcap(BT, w.bits, S - 1) >= want) qcap = qgemm_qcap(BT, w.bits, --S);
     if (qcap < 4 && S > 3) qcap = qgemm_qcap(BT, w.bits, --S);
     while (qcap < 1 && S > 2) qcap = qgemm_qcap(BT, w.bits, --S);
     TS_UNSUPPORTED(qcap >= 1, "qgemm: no shared memory left for the outlier queues");
