@@ -57,7 +57,7 @@ QGEMV_TRAFFIC_BYTES = 31_679_488
 # whether the timed one-GPU step runs as one persistent chained launch (see
 # mlp_step); measured slower than one launch per layer, so kept off
 STEP_CHAIN = False
-QGEMM_TRAFFIC_BYTES = 57_634_816 + 12_308_736
+QGEMM_TRAFFIC_BYTES = 56_665_088 + 8_519_168
 
 
 def peaks():
