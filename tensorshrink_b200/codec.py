@@ -546,22 +546,21 @@ class LayerBitStats:
 
 
 def budget_allocate_bits(stats: Sequence[LayerBitStats], budget_bytes: float) -> Dict[str, int]:
-    """Bit plan under a byte budget, tensorshrink codec.py:997-1033.
+    """Bit plan under a byte budget (same plan as tensorshrink codec.py:997-1033).
 
-    Every layer starts at 4 bits. The bytes left in the budget then buy
-    8-bit upgrades, cheapest error per byte first (ties broken by layer name,
-    larger first, as the reference's tuple sort does); an upgrade that no
-    longer fits is skipped and the next one is tried."""
-    plan = dict.fromkeys((s.name for s in stats), 4)
+    All layers start at 4 bits; the budget left over is spent on 8-bit
+    upgrades in decreasing order of error removed per extra byte (equal
+    ratios keep the order of `stats`), skipping any upgrade that no longer
+    fits. Layers whose 8-bit form is not both larger and more accurate are
+    never upgraded."""
+    plan = {s.name: 4 for s in stats}
     left = budget_bytes - sum(s.bytes4 for s in stats)
-
-    def worth(s: LayerBitStats) -> Tuple[float, str]:
-        return ((s.err4 - s.err8) / (s.bytes8 - s.bytes4), s.name)
-
-    upgradable = [s for s in stats if s.bytes8 > s.bytes4 and s.err4 > s.err8]
-    for s in sorted(upgradable, key=worth, reverse=True):
-        cost = s.bytes8 - s.bytes4
-        if cost <= left:
+    gains = [((s.err4 - s.err8) / (s.bytes8 - s.bytes4), s) for s in stats
+             if s.bytes8 > s.bytes4 and s.err4 > s.err8]
+    gains.sort(key=lambda g: g[0], reverse=True)   # stable: ties stay in input order
+    for _, s in gains:
+        extra = s.bytes8 - s.bytes4
+        if extra <= left:
             plan[s.name] = 8
-            left -= cost
+            left -= extra
     return plan

@@ -120,3 +120,10 @@ def test_hf_config_registered_and_round_trips():
         TensorShrinkConfig(bits=6)
     with pytest.raises(NotImplementedError):
         TensorShrinkConfig(vram_budget_mb=100)
+
+
+def test_budget_ties_keep_input_order():
+    """Equal error-per-byte ratios are upgraded in the order given, as the
+    reference's stable sort on the ratio alone does (codec.py:1025)."""
+    stats = [LayerBitStats("z", 100, 200, 0.2, 0.1), LayerBitStats("a", 100, 200, 0.2, 0.1)]
+    assert budget_allocate_bits(stats, 300) == {"z": 8, "a": 4}
